@@ -1,0 +1,170 @@
+/*
+ * mlora_b200.h — C ABI of the B200 (sm_100a) multi-LoRA hot path.
+ *
+ * Plain pointers and sizes only; every device pointer is a CUDA device
+ * address, every `stream` is a cudaStream_t (NULL = legacy default stream).
+ * No entry point allocates device memory or synchronises the host, so every
+ * one of them may be captured into a CUDA graph.
+ *
+ * Each entry point replaces one operator of the reference project
+ * (Rick0037/multi_lora); the citation is given as file:line within that
+ * project. Return value: MLORA_OK or a negative MLORA_ERR_* code; the message
+ * of the last failure on the calling thread is in mlora_last_error().
+ */
+#ifndef MLORA_B200_H_
+#define MLORA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types (torch.bfloat16 / torch.float16 / torch.float32) */
+#define MLORA_BF16 0
+#define MLORA_F16 1
+#define MLORA_F32 2
+
+/* return codes */
+#define MLORA_OK 0
+#define MLORA_ERR_INVALID_ARGUMENT (-1)
+#define MLORA_ERR_UNSUPPORTED_DTYPE (-2)
+#define MLORA_ERR_CUDA (-3)
+
+/* bits a kernel sets in the optional device status word (uint32) when the
+ * routing metadata would take it out of bounds; the access is skipped. */
+#define MLORA_STATUS_SLOT_RANGE 0x1u    /* weight_indices[i] outside [0, num_slots) */
+#define MLORA_STATUS_RANK_RANGE 0x2u    /* lora_ranks[s] outside [0, max_rank] (clamped) */
+#define MLORA_STATUS_INDPTR 0x4u        /* seg_indptr decreasing or past the row count */
+#define MLORA_STATUS_SCATTER_RANGE 0x8u /* scatter descriptor outside its buffers */
+
+/*
+ * Segment routing of one step; mirrors KernelInputMetaData
+ * (multi_lora/batch_info.py:26-42). All arrays are device int32 except
+ * `scalings`, which has element type `scalings_dtype` (the reference stores
+ * it in the model dtype, batch_info.py:164-165). Segment i covers token rows
+ * [seg_indptr[i], seg_indptr[i+1]) and uses adapter slot weight_indices[i];
+ * slot s has rank lora_ranks[s] (0 = base model, no LoRA) and scaling
+ * scalings[s]. seg_lens is accepted for interface parity and not read: the
+ * boundaries come from seg_indptr, as in backend/torch_backend.py:38-41.
+ */
+typedef struct mlora_kernel_input_metadata {
+  int32_t bs;                     /* number of segments */
+  int32_t max_len;                /* longest segment (host int, as in the reference) */
+  int32_t num_slots;              /* K: slots in the pool (length of lora_ranks/scalings) */
+  int32_t scalings_dtype;         /* MLORA_BF16 / MLORA_F16 / MLORA_F32 */
+  const int32_t* seg_lens;        /* [>= bs] (may be NULL) */
+  const int32_t* seg_indptr;      /* [>= bs + 1] */
+  const int32_t* weight_indices;  /* [>= bs] */
+  const int32_t* lora_ranks;      /* [num_slots] */
+  const void* scalings;           /* [num_slots] */
+} mlora_kernel_input_metadata_t;
+
+/*
+ * Shrink (LoRA A stage): output[t, n] = dtype(sum_k x[t, k] * weights[slot, n, k])
+ * for every token t of a segment routed to `slot` and n < min(max_rank,
+ * lora_ranks[slot] * stack_num); fp32 accumulation. Other columns and rank-0
+ * segments are not written.
+ *   x        [rows, in_dim] of `dtype`, row stride x_row_stride (elements)
+ *   weights  [num_slots, max_rank, in_dim] of `dtype`, contiguous
+ *   output   [rows, >= max_rank], row stride output_row_stride, element type
+ *            `output_dtype` (= dtype, or MLORA_F32 for unrounded partial sums
+ *            that a tensor-parallel all-reduce completes)
+ *   status   optional device uint32 (see MLORA_STATUS_*), may be NULL
+ * Replaces sgemm_lora_a_fwd, multi_lora/kernels/sgemm_lora_a.py:186-274
+ * (called from backend/triton_backend.py:34-45).
+ */
+int mlora_sgemm_lora_a_fwd(const void* x, int64_t rows, int64_t in_dim, int64_t x_row_stride,
+                           const void* weights, int64_t max_rank,
+                           const mlora_kernel_input_metadata_t* meta,
+                           void* output, int64_t output_row_stride, int32_t output_dtype,
+                           int32_t dtype, int32_t stack_num, uint32_t* status, void* stream);
+
+/*
+ * Expand (LoRA B stage), fused scaling and residual add, in place:
+ *   y[t, o] = dtype( dtype(scalings[slot] * sum_{k<rank} mid[t, k] * weights[slot, o, k]) + y[t, o] )
+ *   mid      [rows, >= max_rank] of `mid_dtype` (dtype, or MLORA_F32 partial
+ *            sums, which are rounded to dtype on read)
+ *   weights  [num_slots, out_dim, max_rank] of `dtype`, contiguous
+ *   y        [rows, out_dim] of `dtype`, row stride y_row_stride (a strided
+ *            slice of a wider output is allowed, multi_lora/layers.py:82-83)
+ * Replaces sgemm_lora_b_fwd with base_output given, multi_lora/kernels/
+ * sgemm_lora_b.py:156-236 (backend/triton_backend.py:47-61).
+ */
+int mlora_sgemm_lora_b_fwd(const void* mid, int64_t rows, int64_t mid_row_stride, int32_t mid_dtype,
+                           const void* weights, int64_t out_dim, int64_t max_rank,
+                           const mlora_kernel_input_metadata_t* meta,
+                           void* y, int64_t y_row_stride,
+                           int32_t dtype, uint32_t* status, void* stream);
+
+/*
+ * apply_lora: shrink into `mid`, then expand into y (both launches on
+ * `stream`). Replaces LoRABackend.apply_lora, multi_lora/backend/base.py:60-89.
+ */
+int mlora_apply_lora(const void* x, int64_t rows, int64_t in_dim, int64_t x_row_stride,
+                     const void* a_stack, const void* b_stack, int64_t out_dim, int64_t max_rank,
+                     const mlora_kernel_input_metadata_t* meta,
+                     void* mid, int64_t mid_row_stride,
+                     void* y, int64_t y_row_stride,
+                     int32_t dtype, uint32_t* status, void* stream);
+
+/*
+ * RMSNorm: y[r, :] = dtype( x_f32 * rsqrt(mean(x_f32^2) + eps) * w_f32 ).
+ * Row r of x starts at (r / inner) * stride_outer + (r % inner) * stride_inner
+ * (elements); y is [rows, hidden] with row stride y_row_stride. w has
+ * element type w_dtype. Replaces rmsnorm_fwd, multi_lora/kernels/
+ * rmsnorm.py:48-92 (kernel :18-45).
+ */
+int mlora_rmsnorm_fwd(const void* x, int64_t rows, int64_t hidden, int64_t stride_outer,
+                      int64_t stride_inner, int64_t inner, const void* w, int32_t w_dtype,
+                      void* y, int64_t y_row_stride, float eps, int32_t dtype, void* stream);
+
+/*
+ * One block of a staged adapter bank and where it goes in the slot stacks.
+ * Source: `rows` x `cols` dense elements at `src_offset` within a stage row.
+ * Destination: element [row, col] of slot s lands at
+ *   dst + (s * slot_stride + row * dst_row_stride + col) * element_size.
+ * An A block [rank, in] is (rows=rank, cols=in, dst_row_stride=in) and a B
+ * block [out, rank] is (rows=out, cols=rank, dst_row_stride=max_rank), as in
+ * the offset tables of multi_lora/pool.py:60-94.
+ */
+typedef struct mlora_scatter_rect {
+  int64_t src_offset;
+  int64_t dst;            /* device address of the destination stack's element 0 */
+  int64_t slot_stride;    /* elements between slots */
+  int64_t rows;
+  int64_t cols;
+  int64_t dst_row_stride; /* elements between destination rows */
+} mlora_scatter_rect_t;
+
+/*
+ * Slot load scatter: for every adapter i < h (stage row i, slot slots[i]) and
+ * every rectangle, copy the block from the stage into its slot. `stage` is
+ * [h, stage_row_elems] of `dtype`; `slots` is a device int64 [h]; `rects` a
+ * device array of n_rects descriptors; max_rect_elems bounds rows*cols over
+ * the rectangles (it sizes the grid). A rectangle whose source lies outside
+ * the stage row sets MLORA_STATUS_SCATTER_RANGE and is skipped. The launch
+ * does not overlap the kernels that follow it on `stream`.
+ * Replaces scatter_stage, multi_lora/kernels/scatter_bank.py:68-93
+ * (kernel :18-65), called from pool.py:231-232.
+ */
+int mlora_scatter_stage(const void* stage, int64_t stage_row_elems, int32_t h, const int64_t* slots,
+                        const mlora_scatter_rect_t* rects, int32_t n_rects, int64_t max_rect_elems,
+                        int32_t dtype, uint32_t* status, void* stream);
+
+/* Programmatic dependent launch (on by default; env MLORA_PDL=0 turns it off). */
+void mlora_set_pdl(int enable);
+int mlora_get_pdl(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* mlora_last_error(void);
+
+/* ABI version: major * 10000 + minor * 100 + patch. */
+int mlora_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MLORA_B200_H_ */

@@ -1,0 +1,100 @@
+"""The one backend: hand-written sm_100a kernels behind ``torch.ops.mlora``.
+
+Takes the place of ``TritonLoRABackend`` (multi_lora/backend/triton_backend.py:19-78)
+with the same methods. There is no CPU or Torch fallback: a non-CUDA input or
+a missing extension raises.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from multi_lora_b200 import _native
+from multi_lora_b200.backend.base import LoRABackend
+from multi_lora_b200.batch_info import KernelInputMetaData
+
+
+def _i32(t: torch.Tensor) -> torch.Tensor:
+    return t if t.dtype == torch.int32 and t.is_contiguous() else t.to(torch.int32).contiguous()
+
+
+class CudaLoRABackend(LoRABackend):
+    """Slot-grouped segment shrink/expand on B200 (one launch each per call)."""
+
+    name = "cuda"
+
+    def __init__(self, stack_num: int = 1) -> None:
+        super().__init__()
+        self.stack_num = stack_num
+        self._ops = _native.ops()
+        self._status: Optional[torch.Tensor] = None
+
+    # -- routing-error status word ------------------------------------------
+    def status_word(self, device: torch.device) -> torch.Tensor:
+        """Device int32 word the kernels OR error bits into (see include/mlora_b200.h)."""
+        if self._status is None or self._status.device != device:
+            self._status = torch.zeros(1, dtype=torch.int32, device=device)
+        return self._status
+
+    def check_routing(self) -> None:
+        """Raise if any launch so far met out-of-range routing (synchronises)."""
+        if self._status is None:
+            return
+        bits = int(self._status.item())
+        if bits:
+            self._status.zero_()
+            names = []
+            if bits & 1:
+                names.append("weight_indices outside [0, num_slots)")
+            if bits & 2:
+                names.append("lora_ranks outside [0, max_rank]")
+            if bits & 4:
+                names.append("seg_indptr decreasing or past the row count")
+            if bits & 8:
+                names.append("scatter descriptor out of range")
+            raise RuntimeError("mlora: invalid routing metadata: " + "; ".join(names))
+
+    def _meta(self) -> KernelInputMetaData:
+        meta = self.kernel_input_metadata
+        if meta is None:
+            raise RuntimeError("kernel_input_metadata not set; call set_kernel_input_metadata first")
+        return meta
+
+    def _check_x(self, x: torch.Tensor, what: str) -> torch.Tensor:
+        if not x.is_cuda:
+            raise RuntimeError(f"mlora: {what} must be a CUDA tensor (no CPU path)")
+        if x.dim() != 2:
+            raise ValueError(f"CudaLoRABackend expects {what} [S, n]")
+        return x if x.stride(1) == 1 else x.contiguous()
+
+    def run_lora_a_sgemm(self, x: torch.Tensor, weights: torch.Tensor) -> torch.Tensor:
+        meta = self._meta()
+        x = self._check_x(x, "x")
+        out = self.mid_buffer(x.shape[0], weights.shape[-2], x)
+        return self._ops.sgemm_lora_a(
+            x, weights.contiguous(), _i32(meta.seg_lens), _i32(meta.seg_indptr), _i32(meta.weight_indices),
+            _i32(meta.lora_ranks), int(meta.bs), int(meta.max_len), out, self.stack_num,
+            self.status_word(x.device))
+
+    def run_lora_b_sgemm(
+        self,
+        x: torch.Tensor,
+        weights: torch.Tensor,
+        base_output: Optional[torch.Tensor] = None,
+    ) -> torch.Tensor:
+        meta = self._meta()
+        x = self._check_x(x, "mid")
+        if base_output is None:
+            out = torch.zeros((x.shape[0], weights.shape[-2]), dtype=weights.dtype, device=x.device)
+        else:
+            out = base_output
+        target = out if (out.dim() == 2 and out.stride(1) == 1) else out.contiguous()
+        self._ops.sgemm_lora_b(
+            x, weights.contiguous(), _i32(meta.seg_lens), _i32(meta.seg_indptr), _i32(meta.weight_indices),
+            _i32(meta.lora_ranks), meta.scalings, int(meta.bs), int(meta.max_len), target,
+            self.status_word(x.device))
+        if target is not out:
+            out.copy_(target)
+        return out

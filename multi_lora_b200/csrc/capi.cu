@@ -1,0 +1,227 @@
+// C-ABI entry points (include/mlora_b200.h): argument validation, layout
+// checks that pick the vectorised or scalar kernel, and launch.
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+
+#include "../../include/mlora_b200.h"
+#include "common.cuh"
+#include "kernels.h"
+
+namespace {
+
+thread_local char g_err[512] = {0};
+int g_pdl = -1;  // -1: not read from the environment yet
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return MLORA_OK;
+  return fail(MLORA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool pdl_on() {
+  if (g_pdl < 0) {
+    const char* v = getenv("MLORA_PDL");
+    g_pdl = (v != nullptr && v[0] == '0') ? 0 : 1;
+  }
+  return g_pdl != 0;
+}
+
+int elem_size(int32_t dt) {
+  switch (dt) {
+    case MLORA_BF16:
+    case MLORA_F16: return 2;
+    case MLORA_F32: return 4;
+  }
+  return 0;
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int check_meta(const mlora_kernel_input_metadata_t* m, int64_t rows) {
+  if (m == nullptr) return fail(MLORA_ERR_INVALID_ARGUMENT, "kernel_input_metadata is NULL");
+  if (m->bs < 0) return fail(MLORA_ERR_INVALID_ARGUMENT, "bs must be >= 0 (got %d)", m->bs);
+  if (m->num_slots <= 0) return fail(MLORA_ERR_INVALID_ARGUMENT, "num_slots must be > 0 (got %d)", m->num_slots);
+  if (m->num_slots > 65535) return fail(MLORA_ERR_INVALID_ARGUMENT, "num_slots %d > 65535", m->num_slots);
+  if (m->bs > 0 && (m->seg_indptr == nullptr || m->weight_indices == nullptr))
+    return fail(MLORA_ERR_INVALID_ARGUMENT, "seg_indptr / weight_indices are NULL");
+  if (m->lora_ranks == nullptr) return fail(MLORA_ERR_INVALID_ARGUMENT, "lora_ranks is NULL");
+  if (rows < 0 || rows > INT32_MAX) return fail(MLORA_ERR_INVALID_ARGUMENT, "rows %lld out of range", (long long)rows);
+  return MLORA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* mlora_last_error(void) { return g_err; }
+int mlora_version(void) { return 100; }
+void mlora_set_pdl(int enable) { g_pdl = enable ? 1 : 0; }
+int mlora_get_pdl(void) { return pdl_on() ? 1 : 0; }
+
+int mlora_sgemm_lora_a_fwd(const void* x, int64_t rows, int64_t in_dim, int64_t x_row_stride,
+                           const void* weights, int64_t max_rank,
+                           const mlora_kernel_input_metadata_t* meta,
+                           void* output, int64_t output_row_stride, int32_t output_dtype,
+                           int32_t dtype, int32_t stack_num, uint32_t* status, void* stream) {
+  g_err[0] = 0;
+  if (int rc = check_meta(meta, rows)) return rc;
+  const int es = elem_size(dtype);
+  if (es == 0) return fail(MLORA_ERR_UNSUPPORTED_DTYPE, "unsupported dtype code %d", dtype);
+  const bool out_f32 = output_dtype == MLORA_F32 && dtype != MLORA_F32;
+  if (output_dtype != dtype && !out_f32)
+    return fail(MLORA_ERR_UNSUPPORTED_DTYPE, "output dtype %d must equal dtype %d or be f32", output_dtype, dtype);
+  if (in_dim <= 0 || in_dim > INT32_MAX) return fail(MLORA_ERR_INVALID_ARGUMENT, "in_dim %lld invalid", (long long)in_dim);
+  if (max_rank <= 0 || max_rank > 65535 * 4)
+    return fail(MLORA_ERR_INVALID_ARGUMENT, "max_rank %lld invalid", (long long)max_rank);
+  if (stack_num < 1) return fail(MLORA_ERR_INVALID_ARGUMENT, "stack_num must be >= 1");
+  if (x_row_stride < in_dim) return fail(MLORA_ERR_INVALID_ARGUMENT, "x_row_stride < in_dim");
+  if (output_row_stride < max_rank) return fail(MLORA_ERR_INVALID_ARGUMENT, "output_row_stride < max_rank");
+  if (meta->bs == 0 || rows == 0) return MLORA_OK;
+  if (x == nullptr || weights == nullptr || output == nullptr)
+    return fail(MLORA_ERR_INVALID_ARGUMENT, "x / weights / output is NULL");
+
+  mlora::ShrinkArgs a{};
+  a.x = x;
+  a.x_stride = x_row_stride;
+  a.w = weights;
+  a.w_row_stride = in_dim;
+  a.w_slot_stride = max_rank * in_dim;
+  a.out = output;
+  a.out_stride = output_row_stride;
+  a.seg_indptr = meta->seg_indptr;
+  a.weight_indices = meta->weight_indices;
+  a.lora_ranks = meta->lora_ranks;
+  a.bs = meta->bs;
+  a.S = (int)rows;
+  a.in_dim = (int)in_dim;
+  a.max_rank = (int)max_rank;
+  a.num_slots = meta->num_slots;
+  a.stack_num = stack_num;
+  a.status = status;
+  const int V = 16 / es;
+  a.vec_ok = (in_dim % V == 0) && (x_row_stride % V == 0) && aligned(x, 16) && aligned(weights, 16);
+  return cuda_status(mlora::launch_shrink(a, dtype, out_f32, (cudaStream_t)stream, pdl_on()), "shrink launch");
+}
+
+int mlora_sgemm_lora_b_fwd(const void* mid, int64_t rows, int64_t mid_row_stride, int32_t mid_dtype,
+                           const void* weights, int64_t out_dim, int64_t max_rank,
+                           const mlora_kernel_input_metadata_t* meta,
+                           void* y, int64_t y_row_stride,
+                           int32_t dtype, uint32_t* status, void* stream) {
+  g_err[0] = 0;
+  if (int rc = check_meta(meta, rows)) return rc;
+  const int es = elem_size(dtype);
+  if (es == 0) return fail(MLORA_ERR_UNSUPPORTED_DTYPE, "unsupported dtype code %d", dtype);
+  const bool mid_f32 = mid_dtype == MLORA_F32 && dtype != MLORA_F32;
+  if (mid_dtype != dtype && !mid_f32)
+    return fail(MLORA_ERR_UNSUPPORTED_DTYPE, "mid dtype %d must equal dtype %d or be f32", mid_dtype, dtype);
+  if (elem_size(meta->scalings_dtype) == 0)
+    return fail(MLORA_ERR_UNSUPPORTED_DTYPE, "unsupported scalings dtype %d", meta->scalings_dtype);
+  if (meta->scalings == nullptr) return fail(MLORA_ERR_INVALID_ARGUMENT, "scalings is NULL");
+  if (out_dim <= 0 || out_dim > INT32_MAX) return fail(MLORA_ERR_INVALID_ARGUMENT, "out_dim %lld invalid", (long long)out_dim);
+  if (max_rank <= 0 || max_rank > 65535) return fail(MLORA_ERR_INVALID_ARGUMENT, "max_rank %lld invalid", (long long)max_rank);
+  if (mid_row_stride < max_rank) return fail(MLORA_ERR_INVALID_ARGUMENT, "mid_row_stride < max_rank");
+  if (y_row_stride < out_dim) return fail(MLORA_ERR_INVALID_ARGUMENT, "y_row_stride < out_dim");
+  if (meta->bs == 0 || rows == 0) return MLORA_OK;
+  if (mid == nullptr || weights == nullptr || y == nullptr)
+    return fail(MLORA_ERR_INVALID_ARGUMENT, "mid / weights / y is NULL");
+
+  mlora::ExpandArgs a{};
+  a.mid = mid;
+  a.mid_stride = mid_row_stride;
+  a.w = weights;
+  a.w_row_stride = max_rank;
+  a.w_slot_stride = out_dim * max_rank;
+  a.y = y;
+  a.y_stride = y_row_stride;
+  a.seg_indptr = meta->seg_indptr;
+  a.weight_indices = meta->weight_indices;
+  a.lora_ranks = meta->lora_ranks;
+  a.scalings = meta->scalings;
+  a.scalings_dtype = meta->scalings_dtype;
+  a.bs = meta->bs;
+  a.S = (int)rows;
+  a.out_dim = (int)out_dim;
+  a.max_rank = (int)max_rank;
+  a.num_slots = meta->num_slots;
+  a.status = status;
+  const int V = 16 / es;
+  a.vec_ok = (max_rank % V == 0) && aligned(weights, 16);
+  a.y_vec_ok = (y_row_stride % 2 == 0) && aligned(y, 2 * es);
+  return cuda_status(mlora::launch_expand(a, dtype, mid_f32, (cudaStream_t)stream, pdl_on()), "expand launch");
+}
+
+int mlora_apply_lora(const void* x, int64_t rows, int64_t in_dim, int64_t x_row_stride,
+                     const void* a_stack, const void* b_stack, int64_t out_dim, int64_t max_rank,
+                     const mlora_kernel_input_metadata_t* meta,
+                     void* mid, int64_t mid_row_stride,
+                     void* y, int64_t y_row_stride,
+                     int32_t dtype, uint32_t* status, void* stream) {
+  int rc = mlora_sgemm_lora_a_fwd(x, rows, in_dim, x_row_stride, a_stack, max_rank, meta, mid, mid_row_stride,
+                                  dtype, dtype, 1, status, stream);
+  if (rc != MLORA_OK) return rc;
+  return mlora_sgemm_lora_b_fwd(mid, rows, mid_row_stride, dtype, b_stack, out_dim, max_rank, meta, y,
+                                y_row_stride, dtype, status, stream);
+}
+
+int mlora_rmsnorm_fwd(const void* x, int64_t rows, int64_t hidden, int64_t stride_outer,
+                      int64_t stride_inner, int64_t inner, const void* w, int32_t w_dtype,
+                      void* y, int64_t y_row_stride, float eps, int32_t dtype, void* stream) {
+  g_err[0] = 0;
+  const int es = elem_size(dtype);
+  if (es == 0) return fail(MLORA_ERR_UNSUPPORTED_DTYPE, "unsupported dtype code %d", dtype);
+  if (elem_size(w_dtype) == 0) return fail(MLORA_ERR_UNSUPPORTED_DTYPE, "unsupported weight dtype %d", w_dtype);
+  if (hidden <= 0 || hidden > INT32_MAX) return fail(MLORA_ERR_INVALID_ARGUMENT, "hidden %lld invalid", (long long)hidden);
+  if (rows < 0) return fail(MLORA_ERR_INVALID_ARGUMENT, "rows < 0");
+  if (inner <= 0) return fail(MLORA_ERR_INVALID_ARGUMENT, "inner must be > 0");
+  if (y_row_stride < hidden) return fail(MLORA_ERR_INVALID_ARGUMENT, "y_row_stride < hidden");
+  if (rows == 0) return MLORA_OK;
+  if (x == nullptr || w == nullptr || y == nullptr) return fail(MLORA_ERR_INVALID_ARGUMENT, "x / w / y is NULL");
+  if ((rows + 31) / 32 > 2147483647LL) return fail(MLORA_ERR_INVALID_ARGUMENT, "too many rows");
+
+  mlora::RmsNormArgs a{};
+  a.x = x;
+  a.stride_outer = stride_outer;
+  a.stride_inner = stride_inner;
+  a.inner = inner;
+  a.w = w;
+  a.w_dtype = w_dtype;
+  a.y = y;
+  a.y_stride = y_row_stride;
+  a.rows = rows;
+  a.hidden = (int)hidden;
+  a.eps = eps;
+  const int V = 16 / es;
+  a.vec_ok = (hidden % V == 0) && (stride_outer % V == 0) && (stride_inner % V == 0) && (y_row_stride % V == 0) &&
+             aligned(x, 16) && aligned(y, 16);
+  return cuda_status(mlora::launch_rmsnorm(a, dtype, (cudaStream_t)stream, pdl_on()), "rmsnorm launch");
+}
+
+int mlora_scatter_stage(const void* stage, int64_t stage_row_elems, int32_t h, const int64_t* slots,
+                        const mlora_scatter_rect_t* rects, int32_t n_rects, int64_t max_rect_elems,
+                        int32_t dtype, uint32_t* status, void* stream) {
+  g_err[0] = 0;
+  const int es = elem_size(dtype);
+  if (es == 0) return fail(MLORA_ERR_UNSUPPORTED_DTYPE, "unsupported dtype code %d", dtype);
+  if (h < 0 || n_rects < 0 || stage_row_elems < 0 || max_rect_elems < 0)
+    return fail(MLORA_ERR_INVALID_ARGUMENT, "negative size");
+  if (h == 0 || n_rects == 0 || max_rect_elems == 0) return MLORA_OK;
+  if (h > 65535) return fail(MLORA_ERR_INVALID_ARGUMENT, "h %d > 65535", h);
+  if (stage == nullptr || slots == nullptr || rects == nullptr)
+    return fail(MLORA_ERR_INVALID_ARGUMENT, "stage / slots / rects is NULL");
+  const cudaError_t e = mlora::launch_scatter(stage, stage_row_elems, h, slots, rects, n_rects, max_rect_elems, es,
+                                              status, (cudaStream_t)stream);
+  if (e == cudaErrorInvalidValue) return fail(MLORA_ERR_INVALID_ARGUMENT, "rectangle too large for one launch");
+  return cuda_status(e, "scatter launch");
+}
+
+}  // extern "C"

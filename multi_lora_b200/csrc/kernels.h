@@ -1,0 +1,88 @@
+// Internal launch interface between the C-ABI layer (capi.cu) and the kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <utility>
+
+#include "../../include/mlora_b200.h"
+
+namespace mlora {
+
+struct ShrinkArgs {
+  const void* x;          // [S, in] rows at x_stride elements
+  int64_t x_stride;
+  const void* w;          // A stack: A[s, n, k] = w[s*w_slot_stride + n*w_row_stride + k]
+  int64_t w_slot_stride;
+  int64_t w_row_stride;
+  void* out;              // mid [S, >= max_rank] rows at out_stride elements
+  int64_t out_stride;
+  const int32_t* seg_indptr;      // [bs + 1]
+  const int32_t* weight_indices;  // [bs]
+  const int32_t* lora_ranks;      // [num_slots]
+  int bs, S, in_dim, max_rank, num_slots, stack_num;
+  uint32_t* status;  // optional device status word
+  int vec_ok;        // 128-bit loads legal for x and A
+};
+
+struct ExpandArgs {
+  const void* mid;        // [S, >= max_rank] rows at mid_stride elements
+  int64_t mid_stride;
+  const void* w;          // B stack: B[s, o, k] = w[s*w_slot_stride + o*w_row_stride + k]
+  int64_t w_slot_stride;
+  int64_t w_row_stride;
+  void* y;                // [S, out] rows at y_stride elements, updated in place
+  int64_t y_stride;
+  const int32_t* seg_indptr;
+  const int32_t* weight_indices;
+  const int32_t* lora_ranks;
+  const void* scalings;   // [num_slots] of scalings_dtype
+  int scalings_dtype;
+  int bs, S, out_dim, max_rank, num_slots;
+  uint32_t* status;
+  int vec_ok;    // 128-bit loads legal for B
+  int y_vec_ok;  // paired stores legal for y
+};
+
+struct RmsNormArgs {
+  const void* x;          // row r at (r / inner) * stride_outer + (r % inner) * stride_inner
+  int64_t stride_outer;
+  int64_t stride_inner;
+  int64_t inner;
+  const void* w;          // [hidden] of w_dtype
+  int w_dtype;
+  void* y;                // [rows, hidden] rows at y_stride elements
+  int64_t y_stride;
+  int64_t rows;
+  int hidden;
+  float eps;
+  int vec_ok;
+};
+
+cudaError_t launch_shrink(const ShrinkArgs& a, int dtype, bool out_f32, cudaStream_t st, bool pdl);
+cudaError_t launch_expand(const ExpandArgs& a, int dtype, bool mid_f32, cudaStream_t st, bool pdl);
+cudaError_t launch_rmsnorm(const RmsNormArgs& a, int dtype, cudaStream_t st, bool pdl);
+cudaError_t launch_scatter(const void* stage, int64_t stage_row_elems, int h, const int64_t* slots,
+                           const mlora_scatter_rect_t* rects, int n_rects, int64_t max_rect_elems, int es,
+                           uint32_t* status, cudaStream_t st);
+
+// Launch with the programmatic-stream-serialisation attribute when `pdl`.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_kernel(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                 bool pdl, Args&&... args) {
+  if (grid.x == 0 || grid.y == 0 || grid.z == 0) return cudaSuccess;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
+}
+
+}  // namespace mlora

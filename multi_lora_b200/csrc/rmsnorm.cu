@@ -1,0 +1,140 @@
+// Vectorised one-pass RMSNorm (kernels/rmsnorm.py:18-45,48-92 of the reference):
+//   y[r, :] = T( (x_f32 * rsqrt(sum(x_f32^2) / H + eps)) * w_f32 )
+// Rows are addressed with the reference's two-level stride
+// (row r -> (r / inner) * stride_outer + (r % inner) * stride_inner,
+// rmsnorm.py:59-74) so the q/k column slices of a fused qkv output are read in
+// place. A group of G threads owns one row; each thread keeps its CPT chunks of
+// the row in registers, so x is read from HBM exactly once. The norm weight is
+// loaded before griddepcontrol.wait (it is constant for the step).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace mlora {
+
+template <typename T, int V, int NT, int G, int CPT>
+__global__ void __launch_bounds__(NT) rmsnorm_kernel(const RmsNormArgs p) {
+  constexpr int RPB = NT / G;       // rows per block
+  constexpr int WPG = G / 32;       // warps per row group
+  __shared__ float s_part[RPB][WPG > 0 ? WPG : 1];
+
+  const int tid = threadIdx.x;
+  const int grp = tid / G, gt = tid % G;
+  const int lane = tid & 31, wig = gt >> 5;
+  const int64_t row = (int64_t)blockIdx.x * RPB + grp;
+  const bool row_ok = row < p.rows;
+  const int nchunk = p.hidden / V;
+  constexpr int BLK = G * CPT;
+  const int nblk = (nchunk + BLK - 1) / BLK;
+
+  // norm weight (stable): converted once to fp32 per chunk
+  float wf[CPT][V];
+  auto load_w = [&](int blk) {
+#pragma unroll
+    for (int j = 0; j < CPT; ++j) {
+      const int c = blk * BLK + j * G + gt;
+#pragma unroll
+      for (int e = 0; e < V; ++e) wf[j][e] = 0.f;
+      if (c < nchunk) {
+        const int64_t k = (int64_t)c * V;
+#pragma unroll
+        for (int e = 0; e < V; ++e) {
+          float v;
+          switch (p.w_dtype) {
+            case kBF16: v = __bfloat162float(__ldg(static_cast<const __nv_bfloat16*>(p.w) + k + e)); break;
+            case kF16: v = __half2float(__ldg(static_cast<const __half*>(p.w) + k + e)); break;
+            default: v = __ldg(static_cast<const float*>(p.w) + k + e); break;
+          }
+          wf[j][e] = v;
+        }
+      }
+    }
+  };
+  if (nblk == 1) load_w(0);
+  pdl_trigger();
+  pdl_wait();
+
+  const T* xr = static_cast<const T*>(p.x);
+  if (row_ok) xr += (row / p.inner) * p.stride_outer + (row % p.inner) * p.stride_inner;
+  T* yr = static_cast<T*>(p.y) + (row_ok ? row * p.y_stride : 0);
+
+  Chunk<T, V> xc[CPT];
+  float ss = 0.f;
+  for (int blk = 0; blk < nblk; ++blk) {
+#pragma unroll
+    for (int j = 0; j < CPT; ++j) {
+      const int c = blk * BLK + j * G + gt;
+      if (row_ok && c < nchunk) xc[j].ldcg(xr + (int64_t)c * V); else xc[j].zero();
+      float f[V];
+      xc[j].to_f(f);
+#pragma unroll
+      for (int e = 0; e < V; ++e) ss = fmaf(f[e], f[e], ss);
+    }
+  }
+  ss = warp_sum(ss);
+  if constexpr (WPG > 1) {
+    if (lane == 0) s_part[grp][wig] = ss;
+    __syncthreads();
+    ss = 0.f;
+#pragma unroll
+    for (int w = 0; w < WPG; ++w) ss += s_part[grp][w];
+  }
+  // Reference: var = sum / n_cols; rstd = rsqrt(var + eps)  (rmsnorm.py:40-41)
+  const float rstd = rsqrtf(ss / (float)p.hidden + p.eps);
+  if (!row_ok) return;
+
+  for (int blk = 0; blk < nblk; ++blk) {
+    if (nblk > 1) load_w(blk);
+#pragma unroll
+    for (int j = 0; j < CPT; ++j) {
+      const int c = blk * BLK + j * G + gt;
+      if (c >= nchunk) continue;
+      if (nblk > 1) xc[j].ldcg(xr + (int64_t)c * V);
+      float f[V];
+      xc[j].to_f(f);
+      if constexpr (V * sizeof(T) == 16) {
+        T o[V];
+#pragma unroll
+        for (int e = 0; e < V; ++e) o[e] = Num<T>::from_f((f[e] * rstd) * wf[j][e]);
+        uint4 u;
+        memcpy(&u, o, 16);
+        *reinterpret_cast<uint4*>(yr + (int64_t)c * V) = u;
+      } else {
+#pragma unroll
+        for (int e = 0; e < V; ++e) yr[(int64_t)c * V + e] = Num<T>::from_f((f[e] * rstd) * wf[j][e]);
+      }
+    }
+  }
+}
+
+namespace {
+
+template <typename T, int V>
+cudaError_t rms_dispatch(const RmsNormArgs& a, cudaStream_t st, bool pdl) {
+  const int nchunk = a.hidden / V;
+  auto go = [&](auto kern, int nt, int g) {
+    const int rpb = nt / g;
+    const dim3 grid((unsigned)((a.rows + rpb - 1) / rpb));
+    return launch_kernel(kern, grid, dim3(nt), 0, st, pdl, a);
+  };
+  if (nchunk <= 32) return go(rmsnorm_kernel<T, V, 256, 32, 1>, 256, 32);
+  if (nchunk <= 64) return go(rmsnorm_kernel<T, V, 256, 32, 2>, 256, 32);
+  if (nchunk <= 128) return go(rmsnorm_kernel<T, V, 256, 32, 4>, 256, 32);
+  if (nchunk <= 256) return go(rmsnorm_kernel<T, V, 256, 64, 4>, 256, 64);
+  if (nchunk <= 512) return go(rmsnorm_kernel<T, V, 256, 128, 4>, 256, 128);
+  if (nchunk <= 1024) return go(rmsnorm_kernel<T, V, 256, 256, 4>, 256, 256);
+  if (nchunk <= 2048) return go(rmsnorm_kernel<T, V, 512, 512, 4>, 512, 512);
+  return go(rmsnorm_kernel<T, V, 1024, 1024, 4>, 1024, 1024);  // loops blocks past 4096 chunks
+}
+
+}  // namespace
+
+cudaError_t launch_rmsnorm(const RmsNormArgs& a, int dtype, cudaStream_t st, bool pdl) {
+  switch (dtype) {
+    case kBF16: return a.vec_ok ? rms_dispatch<__nv_bfloat16, 8>(a, st, pdl) : rms_dispatch<__nv_bfloat16, 1>(a, st, pdl);
+    case kF16: return a.vec_ok ? rms_dispatch<__half, 8>(a, st, pdl) : rms_dispatch<__half, 1>(a, st, pdl);
+    case kF32: return a.vec_ok ? rms_dispatch<float, 4>(a, st, pdl) : rms_dispatch<float, 1>(a, st, pdl);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace mlora

@@ -1,0 +1,195 @@
+// torch.ops.mlora.* — a thin PyTorch binding over the C ABI (include/mlora_b200.h).
+// Checks what the reference asserts (kernels/sgemm_lora_a.py:199-208,
+// sgemm_lora_b.py:168-174: contiguous rank-2 x / rank-3 weights) plus dtype,
+// device and metadata-length checks, then forwards device pointers and the
+// current CUDA stream. No op allocates except rmsnorm (whose reference
+// allocates its output, kernels/rmsnorm.py:76); rmsnorm_out writes in place.
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/library.h>
+
+#include "../../include/mlora_b200.h"
+
+namespace {
+
+int32_t dt_code(at::ScalarType t) {
+  switch (t) {
+    case at::kBFloat16: return MLORA_BF16;
+    case at::kHalf: return MLORA_F16;
+    case at::kFloat: return MLORA_F32;
+    default: TORCH_CHECK(false, "mlora: unsupported dtype ", t);
+  }
+  return -1;
+}
+
+void check_cuda(const at::Tensor& t, const char* name, const at::Device& dev) {
+  TORCH_CHECK(t.is_cuda(), "mlora: ", name, " must be a CUDA tensor");
+  TORCH_CHECK(t.device() == dev, "mlora: ", name, " is on ", t.device(), ", expected ", dev);
+}
+
+void check_i32(const at::Tensor& t, const char* name, int64_t min_len, const at::Device& dev) {
+  check_cuda(t, name, dev);
+  TORCH_CHECK(t.scalar_type() == at::kInt, "mlora: ", name, " must be int32 (got ", t.scalar_type(), ")");
+  TORCH_CHECK(t.dim() == 1 && t.is_contiguous(), "mlora: ", name, " must be a contiguous 1-D tensor");
+  TORCH_CHECK(t.numel() >= min_len, "mlora: ", name, " has ", t.numel(), " entries, needs >= ", min_len);
+}
+
+uint32_t* status_ptr(const c10::optional<at::Tensor>& status, const at::Device& dev) {
+  if (!status.has_value()) return nullptr;
+  const at::Tensor& s = *status;
+  check_cuda(s, "status", dev);
+  TORCH_CHECK(s.scalar_type() == at::kInt && s.numel() >= 1, "mlora: status must be an int32 tensor");
+  return reinterpret_cast<uint32_t*>(s.data_ptr());
+}
+
+mlora_kernel_input_metadata_t make_meta(const at::Tensor& seg_lens, const at::Tensor& seg_indptr,
+                                        const at::Tensor& weight_indices, const at::Tensor& lora_ranks,
+                                        const at::Tensor* scalings, int64_t bs, int64_t max_len,
+                                        const at::Device& dev) {
+  TORCH_CHECK(bs >= 0, "mlora: bs must be >= 0");
+  check_i32(seg_indptr, "seg_indptr", bs + 1, dev);
+  check_i32(weight_indices, "weight_indices", bs, dev);
+  check_i32(lora_ranks, "lora_ranks", 1, dev);
+  if (seg_lens.defined() && seg_lens.numel() > 0) check_i32(seg_lens, "seg_lens", bs, dev);
+  mlora_kernel_input_metadata_t m{};
+  m.bs = (int32_t)bs;
+  m.max_len = (int32_t)max_len;
+  m.num_slots = (int32_t)lora_ranks.numel();
+  m.seg_lens = seg_lens.defined() && seg_lens.numel() > 0 ? seg_lens.data_ptr<int32_t>() : nullptr;
+  m.seg_indptr = seg_indptr.data_ptr<int32_t>();
+  m.weight_indices = weight_indices.data_ptr<int32_t>();
+  m.lora_ranks = lora_ranks.data_ptr<int32_t>();
+  if (scalings != nullptr) {
+    check_cuda(*scalings, "scalings", dev);
+    TORCH_CHECK(scalings->dim() == 1 && scalings->is_contiguous(), "mlora: scalings must be contiguous 1-D");
+    TORCH_CHECK(scalings->numel() >= m.num_slots, "mlora: scalings shorter than lora_ranks");
+    m.scalings = scalings->data_ptr();
+    m.scalings_dtype = dt_code(scalings->scalar_type());
+  }
+  return m;
+}
+
+void check_rc(int rc) { TORCH_CHECK(rc == MLORA_OK, "mlora: ", mlora_last_error()); }
+
+at::Tensor sgemm_lora_a(const at::Tensor& x, const at::Tensor& weights, const at::Tensor& seg_lens,
+                        const at::Tensor& seg_indptr, const at::Tensor& weight_indices,
+                        const at::Tensor& lora_ranks, int64_t bs, int64_t max_len, at::Tensor output,
+                        int64_t stack_num, const c10::optional<at::Tensor>& status) {
+  const at::Device dev = x.device();
+  check_cuda(x, "x", dev);
+  check_cuda(weights, "weights", dev);
+  check_cuda(output, "output", dev);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "mlora: x must be [S, in] with unit column stride");
+  TORCH_CHECK(weights.dim() == 3 && weights.is_contiguous(), "mlora: weights must be contiguous [K, max_rank, in]");
+  TORCH_CHECK(weights.size(2) == x.size(1), "mlora: weights in_dim ", weights.size(2), " != x in_dim ", x.size(1));
+  TORCH_CHECK(weights.scalar_type() == x.scalar_type(), "mlora: weights dtype must match x");
+  TORCH_CHECK(output.dim() == 2 && output.stride(1) == 1, "mlora: output must be 2-D with unit column stride");
+  TORCH_CHECK(output.size(0) >= x.size(0) && output.size(1) >= weights.size(1),
+              "mlora: output ", output.sizes(), " too small for [", x.size(0), ", ", weights.size(1), "]");
+  TORCH_CHECK(lora_ranks.numel() == weights.size(0), "mlora: lora_ranks length != number of slots");
+  const c10::cuda::CUDAGuard guard(dev);
+  const auto meta = make_meta(seg_lens, seg_indptr, weight_indices, lora_ranks, nullptr, bs, max_len, dev);
+  const int rc = mlora_sgemm_lora_a_fwd(
+      x.data_ptr(), x.size(0), x.size(1), x.stride(0), weights.data_ptr(), weights.size(1), &meta,
+      output.data_ptr(), output.stride(0), dt_code(output.scalar_type()), dt_code(x.scalar_type()),
+      (int32_t)stack_num, status_ptr(status, dev), at::cuda::getCurrentCUDAStream().stream());
+  check_rc(rc);
+  return output;
+}
+
+at::Tensor sgemm_lora_b(const at::Tensor& x, const at::Tensor& weights, const at::Tensor& seg_lens,
+                        const at::Tensor& seg_indptr, const at::Tensor& weight_indices,
+                        const at::Tensor& lora_ranks, const at::Tensor& scalings, int64_t bs, int64_t max_len,
+                        at::Tensor output, const c10::optional<at::Tensor>& status) {
+  const at::Device dev = x.device();
+  check_cuda(x, "x", dev);
+  check_cuda(weights, "weights", dev);
+  check_cuda(output, "output", dev);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "mlora: mid must be [S, max_rank] with unit column stride");
+  TORCH_CHECK(weights.dim() == 3 && weights.is_contiguous(), "mlora: weights must be contiguous [K, out, max_rank]");
+  TORCH_CHECK(x.size(1) >= weights.size(2), "mlora: mid has ", x.size(1), " columns, weights rank ", weights.size(2));
+  TORCH_CHECK(output.dim() == 2 && output.stride(1) == 1, "mlora: output must be 2-D with unit column stride");
+  TORCH_CHECK(output.size(1) == weights.size(1), "mlora: output width ", output.size(1), " != out_dim ", weights.size(1));
+  TORCH_CHECK(output.size(0) == x.size(0), "mlora: output rows != mid rows");
+  TORCH_CHECK(weights.scalar_type() == output.scalar_type(), "mlora: weights dtype must match output");
+  TORCH_CHECK(lora_ranks.numel() == weights.size(0), "mlora: lora_ranks length != number of slots");
+  const c10::cuda::CUDAGuard guard(dev);
+  const auto meta = make_meta(seg_lens, seg_indptr, weight_indices, lora_ranks, &scalings, bs, max_len, dev);
+  const int rc = mlora_sgemm_lora_b_fwd(
+      x.data_ptr(), x.size(0), x.stride(0), dt_code(x.scalar_type()), weights.data_ptr(), weights.size(1),
+      weights.size(2), &meta, output.data_ptr(), output.stride(0), dt_code(output.scalar_type()),
+      status_ptr(status, dev), at::cuda::getCurrentCUDAStream().stream());
+  check_rc(rc);
+  return output;
+}
+
+// Two-level row addressing of the reference (kernels/rmsnorm.py:59-81).
+void rms_layout(const at::Tensor& x, int64_t hidden, int64_t rows, int64_t& so, int64_t& si, int64_t& inner,
+                at::Tensor& src) {
+  src = x;
+  if (x.is_contiguous()) {
+    inner = rows > 0 ? rows : 1;
+    so = 0;
+    si = hidden;
+  } else if (x.dim() >= 2 && x[0].is_contiguous() && x.stride(-1) == 1) {
+    inner = rows / x.size(0);
+    so = x.stride(0);
+    si = hidden;
+    if (inner == 0) inner = 1;
+  } else {
+    src = x.contiguous();
+    inner = rows > 0 ? rows : 1;
+    so = 0;
+    si = hidden;
+  }
+}
+
+at::Tensor rmsnorm_out(const at::Tensor& x, const at::Tensor& weight, double eps, at::Tensor out) {
+  const at::Device dev = x.device();
+  check_cuda(x, "x", dev);
+  check_cuda(weight, "weight", dev);
+  check_cuda(out, "out", dev);
+  const int64_t hidden = x.size(-1);
+  TORCH_CHECK(weight.numel() == hidden && weight.is_contiguous(), "mlora: weight must be contiguous [hidden]");
+  TORCH_CHECK(out.scalar_type() == x.scalar_type() && out.is_contiguous() && out.numel() == x.numel(),
+              "mlora: out must be a contiguous tensor like x");
+  const int64_t rows = hidden > 0 ? x.numel() / hidden : 0;
+  if (rows == 0) return out;
+  int64_t so, si, inner;
+  at::Tensor src;
+  rms_layout(x, hidden, rows, so, si, inner, src);
+  const c10::cuda::CUDAGuard guard(dev);
+  const int rc = mlora_rmsnorm_fwd(src.data_ptr(), rows, hidden, so, si, inner, weight.data_ptr(),
+                                   dt_code(weight.scalar_type()), out.data_ptr(), hidden, (float)eps,
+                                   dt_code(x.scalar_type()), at::cuda::getCurrentCUDAStream().stream());
+  check_rc(rc);
+  return out;
+}
+
+at::Tensor rmsnorm(const at::Tensor& x, const at::Tensor& weight, double eps) {
+  at::Tensor out = at::empty(x.sizes(), x.options().memory_format(at::MemoryFormat::Contiguous));
+  return rmsnorm_out(x, weight, eps, out);
+}
+
+}  // namespace
+
+TORCH_LIBRARY(mlora, m) {
+  m.def(
+      "sgemm_lora_a(Tensor x, Tensor weights, Tensor seg_lens, Tensor seg_indptr, Tensor weight_indices, "
+      "Tensor lora_ranks, int bs, int max_len, Tensor(a!) output, int stack_num=1, Tensor(b!)? status=None) "
+      "-> Tensor(a!)");
+  m.def(
+      "sgemm_lora_b(Tensor x, Tensor weights, Tensor seg_lens, Tensor seg_indptr, Tensor weight_indices, "
+      "Tensor lora_ranks, Tensor scalings, int bs, int max_len, Tensor(a!) output, Tensor(b!)? status=None) "
+      "-> Tensor(a!)");
+  m.def("rmsnorm(Tensor x, Tensor weight, float eps) -> Tensor");
+  m.def("rmsnorm_out(Tensor x, Tensor weight, float eps, Tensor(a!) out) -> Tensor(a!)");
+}
+
+TORCH_LIBRARY_IMPL(mlora, CUDA, m) {
+  m.impl("sgemm_lora_a", &sgemm_lora_a);
+  m.impl("sgemm_lora_b", &sgemm_lora_b);
+  m.impl("rmsnorm", &rmsnorm);
+  m.impl("rmsnorm_out", &rmsnorm_out);
+}
