@@ -1,0 +1,242 @@
+"""Parity of the CUDA shrink/expand kernels, called through the C ABI, against the
+oracle and the reference's golden vectors.
+
+Tolerances: fp32 paths 1e-5 (accumulation order only); bf16/fp16 outputs within
+max-abs 2e-2 and relative 1e-2 of the fp32-accumulated per-segment reference
+(the bound stated for this path), and within 2 ulp of the reference's own
+bf16 Torch backend where golden vectors exist.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import capi_helpers as C
+from conftest import load_npz
+from multi_lora_b200 import _native
+from oracle import lora_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL = 2e-2, 1e-2
+
+
+def _to(a, dev, dtype=torch.float32):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev, dtype)
+
+
+@pytest.mark.parametrize("name, key", [("toy_f32.npz", "torch"), ("toy_f32.npz", "triton"),
+                                       ("decode_f32.npz", "torch"), ("decode_f32.npz", "triton")])
+def test_fp32_matches_reference_golden(cuda_dev, name, key):
+    z = load_npz(name)
+    x, A, B, y = (_to(z[k], cuda_dev) for k in ("x", "A", "B", "y"))
+    meta = C.meta_from_npz(z, cuda_dev)
+    mid = torch.zeros(x.shape[0], A.shape[1], device=cuda_dev)
+    C.check(C.shrink(x, A, meta, mid))
+    C.check(C.expand(mid, B, meta, y))
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(C.f32(mid), z[f"mid_{key}"][:, :A.shape[1]], rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(C.f32(y), z[f"y_{key}"], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("case", ["prefill", "decode"])
+def test_bf16_matches_reference_torch_backend(cuda_dev, case):
+    z = load_npz("torch_bf16.npz")
+    bf = lambda k: _to(O.bf16_from_bits(z[k]), cuda_dev, torch.bfloat16)  # noqa: E731
+    A, B, x, y = bf("A"), bf("B"), bf(f"{case}_x"), bf(f"{case}_y")
+    meta = C.meta_from_npz(z, cuda_dev, f"{case}_", scal_dtype=torch.bfloat16)
+    mid = torch.zeros(x.shape[0], A.shape[1], device=cuda_dev, dtype=torch.bfloat16)
+    C.check(C.shrink(x, A, meta, mid))
+    C.check(C.expand(mid, B, meta, y))
+    torch.cuda.synchronize()
+    ref_mid = O.bf16_from_bits(z[f"{case}_mid"])
+    ref_out = O.bf16_from_bits(z[f"{case}_out"])
+    np.testing.assert_allclose(C.f32(mid), ref_mid, rtol=2 ** -7, atol=1e-6)
+    np.testing.assert_allclose(C.f32(y), ref_out, rtol=2 ** -6, atol=2 ** -7)
+    ind, widx, ranks, scal, bs = (z[f"{case}_seg_indptr"], z[f"{case}_weight_indices"], z[f"{case}_lora_ranks"],
+                                  z[f"{case}_scalings"], int(z[f"{case}_bs"]))
+    want = O.apply_lora_fp32(O.bf16_from_bits(z[f"{case}_x"]), O.bf16_from_bits(z["A"]), O.bf16_from_bits(z["B"]),
+                             ind, widx, ranks, scal, bs, O.bf16_from_bits(z[f"{case}_y"]))
+    np.testing.assert_allclose(C.f32(y), want, rtol=RTOL, atol=ATOL)
+
+
+def _case(seed, dtype, n_in, n_out, R, ranks, lens, dev, nan_tails=True, y_pad=(1, 8)):
+    g = torch.Generator().manual_seed(seed)
+    K = len(ranks)
+    S = sum(lens)
+    widx = torch.randint(0, K, (len(lens),), generator=g).tolist()
+    scal = [float(0.5 + (i % 4) * 0.5) for i in range(K)]
+    x = torch.randn(S, n_in, generator=g).to(dtype)
+    A = (torch.randn(K, R, n_in, generator=g) * n_in ** -0.5).to(dtype)
+    B = (torch.randn(K, n_out, R, generator=g) * 0.05).to(dtype)
+    if nan_tails:  # weights past each slot's rank are stale in the pool; must never be read
+        for s, r in enumerate(ranks):
+            A[s, r:] = float("nan")
+            B[s, :, r:] = float("nan")
+    ybase = torch.randn(S, n_out, generator=g).to(dtype)
+    # y lives inside a larger buffer with a sentinel border (guard band)
+    big = torch.full((S + 2 * y_pad[0], n_out + 2 * y_pad[1]), 7.0, dtype=dtype)
+    big[y_pad[0]:y_pad[0] + S, y_pad[1]:y_pad[1] + n_out] = ybase
+    return dict(x=x.to(dev), A=A.to(dev), B=B.to(dev), ybase=ybase, big=big.to(dev), widx=widx, scal=scal,
+                lens=lens, ranks=ranks, pad=y_pad)
+
+
+def _check_case(c, dev, dtype, scal_dtype=torch.float32):
+    S = c["x"].shape[0]
+    R = c["A"].shape[1]
+    n_out = c["B"].shape[1]
+    meta = C.make_meta(c["lens"], c["widx"], c["ranks"], c["scal"], dev, scal_dtype)
+    mid_big = torch.full((S, R + 4), -3.0, dtype=dtype, device=dev)  # columns past rank keep the sentinel
+    mid = mid_big[:, :R]
+    p0, p1 = c["pad"]
+    y = c["big"][p0:p0 + S, p1:p1 + n_out]
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    C.check(C.shrink(c["x"], c["A"], meta, mid, status=status))
+    C.check(C.expand(mid, c["B"], meta, y, status=status))
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    ind = meta.seg_indptr.cpu().numpy()
+    want = O.apply_lora_fp32(C.f32(c["x"]), np.nan_to_num(C.f32(c["A"])), np.nan_to_num(C.f32(c["B"])), ind,
+                             c["widx"], c["ranks"], [float(torch.tensor(s, dtype=scal_dtype)) for s in c["scal"]],
+                             len(c["lens"]), C.f32(c["ybase"]))
+    got = C.f32(y)
+    assert np.isfinite(got).all()
+    tol = (1e-4, 1e-4) if dtype == torch.float32 else (RTOL, ATOL)
+    np.testing.assert_allclose(got, want, rtol=tol[0], atol=tol[1])
+    # guard band untouched
+    big = C.f32(c["big"])
+    inner = np.zeros(big.shape, bool)
+    inner[p0:p0 + S, p1:p1 + n_out] = True
+    assert (big[~inner] == 7.0).all()
+    # mid: columns >= rank (and whole rank-0 / empty segments) untouched
+    m = C.f32(mid_big)
+    assert (m[:, R:] == -3.0).all()
+    for seg, slot in enumerate(c["widx"]):
+        r = c["ranks"][slot]
+        rows = slice(ind[seg], ind[seg + 1])
+        assert (m[rows, r:R] == -3.0).all()
+        mid_want = O.shrink(C.f32(c["x"])[rows], np.nan_to_num(C.f32(c["A"]))[[slot]], [0, rows.stop - rows.start],
+                            [0], [r], 1, "f32")
+        tol_m = 1e-4 if dtype == torch.float32 else 1e-2
+        np.testing.assert_allclose(m[rows, :r], mid_want[:, :r], rtol=tol_m, atol=tol_m)
+
+
+SHAPES = [
+    # n_in, n_out, R, ranks, lens
+    (4096, 4096, 16, [16] * 6, [1] * 24),                       # decode, cfg2-like module
+    (4096, 11008, 16, [16, 16, 0, 16], [1] * 16),               # gate/up width, base slot
+    (11008, 4096, 16, [16, 16, 16], [1] * 12),                  # down in-dim
+    (1024, 1000, 64, [0, 8, 64, 17, 32], [1] * 20),             # mixed ranks incl. odd rank, out % 256 != 0
+    (512, 384, 64, [8, 64, 16], [5, 1, 7, 3, 2, 0, 9]),         # prefill segments incl. an empty one
+    (100, 72, 20, [20, 4, 9], [3, 1, 4]),                       # unaligned in/out/R: scalar paths
+    (256, 256, 8, [8, 8, 8, 8], [1, 3, 5, 2, 7, 4]),            # cfg1 shape
+    (2048, 2048, 16, [16] * 3, [40, 25, 33]),                   # many tokens per slot (> tile)
+    (28672 // 8, 8192 // 8, 16, [16] * 8, [1] * 32),            # cfg5 TP8 down shard
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: f"{s[0]}x{s[1]}r{s[2]}")
+def test_random_cases_match_oracle(cuda_dev, dtype, shape):
+    n_in, n_out, R, ranks, lens = shape
+    c = _case(hash((n_in, n_out, R)) % 1000, dtype, n_in, n_out, R, ranks, lens, cuda_dev)
+    _check_case(c, cuda_dev, dtype)
+
+
+def test_many_segments_more_than_one_pass(cuda_dev):
+    """bs above the per-pass segment capacity (256) for one slot."""
+    lens = [1] * 700
+    c = _case(5, torch.bfloat16, 512, 640, 16, [16, 16], lens, cuda_dev)
+    _check_case(c, cuda_dev, torch.bfloat16)
+
+
+def test_bf16_scalings_dtype(cuda_dev):
+    c = _case(7, torch.bfloat16, 1024, 512, 16, [16, 8, 16], [1] * 10, cuda_dev)
+    _check_case(c, cuda_dev, torch.bfloat16, scal_dtype=torch.bfloat16)
+
+
+def test_fp32_partial_mid_equals_rounded_path(cuda_dev):
+    """Shrink into f32 partial sums + expand reading f32 mid == the bf16-mid path, bit for bit."""
+    c = _case(11, torch.bfloat16, 2048, 1024, 16, [16, 16, 8], [1] * 12, cuda_dev, nan_tails=False)
+    meta = C.make_meta(c["lens"], c["widx"], c["ranks"], c["scal"], cuda_dev)
+    S = c["x"].shape[0]
+    mid_b = torch.zeros(S, 16, dtype=torch.bfloat16, device=cuda_dev)
+    mid_f = torch.zeros(S, 16, dtype=torch.float32, device=cuda_dev)
+    y1 = c["ybase"].to(cuda_dev).clone()
+    y2 = c["ybase"].to(cuda_dev).clone()
+    C.check(C.shrink(c["x"], c["A"], meta, mid_b))
+    C.check(C.shrink(c["x"], c["A"], meta, mid_f))
+    C.check(C.expand(mid_b, c["B"], meta, y1))
+    C.check(C.expand(mid_f, c["B"], meta, y2))
+    torch.cuda.synchronize()
+    assert torch.equal(mid_f.bfloat16(), mid_b)
+    assert torch.equal(y1, y2)
+
+
+def test_stack_num(cuda_dev):
+    """stack_num widens the written rows to rank * stack_num (sgemm_lora_a.py:51)."""
+    dev = cuda_dev
+    g = torch.Generator().manual_seed(3)
+    K, R, n_in, S = 3, 48, 256, 6
+    ranks = [8, 16, 4]
+    A = torch.randn(K, R, n_in, generator=g).bfloat16().to(dev)
+    x = torch.randn(S, n_in, generator=g).bfloat16().to(dev)
+    meta = C.make_meta([2, 1, 3], [0, 1, 2], ranks, [1.0] * K, dev)
+    mid = torch.full((S, R), -5.0, dtype=torch.bfloat16, device=dev)
+    C.check(C.shrink(x, A, meta, mid, stack_num=3))
+    torch.cuda.synchronize()
+    m = C.f32(mid)
+    ind = [0, 2, 3, 6]
+    for seg, slot in enumerate([0, 1, 2]):
+        n = min(R, ranks[slot] * 3)
+        want = C.f32(x)[ind[seg]:ind[seg + 1]] @ C.f32(A)[slot, :n].T
+        np.testing.assert_allclose(m[ind[seg]:ind[seg + 1], :n], want, rtol=1e-2, atol=1e-2)
+        assert (m[ind[seg]:ind[seg + 1], n:] == -5.0).all()
+
+
+def test_invalid_routing_sets_status_and_skips(cuda_dev):
+    """Out-of-range slot / indptr / rank are reported in the status word; nothing is written."""
+    dev = cuda_dev
+    x = torch.randn(4, 64, device=dev).bfloat16()
+    A = torch.randn(2, 16, 64, device=dev).bfloat16()
+    B = torch.randn(2, 128, 16, device=dev).bfloat16()
+    cases = {
+        1: C.make_meta([1, 1], [0, 5], [16, 16], [1.0, 1.0], dev),                     # slot 5 of 2
+        4: C.make_meta([1, 1], [0, 1], [16, 16], [1.0, 1.0], dev, indptr=[0, 1, 9]),   # past S=4
+        2: C.make_meta([1, 1], [0, 1], [16, 99], [1.0, 1.0], dev),                     # rank > max_rank (clamped)
+    }
+    for bit, meta in cases.items():
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        mid = torch.zeros(4, 16, dtype=torch.bfloat16, device=dev)
+        y = torch.zeros(4, 128, dtype=torch.bfloat16, device=dev)
+        C.check(C.shrink(x, A, meta, mid, status=status))
+        C.check(C.expand(mid, B, meta, y, status=status))
+        torch.cuda.synchronize()
+        assert int(status.item()) & bit, (bit, int(status.item()))
+
+
+def test_pdl_on_and_off_agree(cuda_dev):
+    c = _case(13, torch.bfloat16, 4096, 4096, 16, [16] * 8, [1] * 32, cuda_dev, nan_tails=False)
+    meta = C.make_meta(c["lens"], c["widx"], c["ranks"], c["scal"], cuda_dev)
+    outs = []
+    old = _native.get_pdl()
+    for pdl in (True, False):
+        _native.set_pdl(pdl)
+        mid = torch.zeros(32, 16, dtype=torch.bfloat16, device=cuda_dev)
+        y = c["ybase"].to(cuda_dev).clone()
+        C.check(C.apply_lora(c["x"], c["A"], c["B"], meta, mid, y))
+        torch.cuda.synchronize()
+        outs.append(y)
+    _native.set_pdl(old)
+    assert torch.equal(outs[0], outs[1])
+
+
+def test_empty_batch_is_noop(cuda_dev):
+    x = torch.randn(0, 64, device=cuda_dev).bfloat16()
+    A = torch.randn(2, 16, 64, device=cuda_dev).bfloat16()
+    meta = C.make_meta([], [], [16, 16], [1.0, 1.0], cuda_dev)
+    mid = torch.zeros(0, 16, dtype=torch.bfloat16, device=cuda_dev)
+    C.check(C.shrink(x, A, meta, mid))
+    torch.cuda.synchronize()

@@ -1,0 +1,103 @@
+"""Slot-pool loads on the GPU (pinned bank -> stage -> scatter kernel), bit-exact.
+
+* against the reference pool's slot contents (golden, PYTHONHASHSEED=0);
+* the reference GPU test's rounds (test_pool_write_many_gpu.py:65-94), including
+  more same-rank adapters than one scatter chunk, missing modules and slot reuse.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_json, load_npz, rerun_under_hashseed0
+from multi_lora_b200.pool import _BANK_CHUNK, LoRAMemoryPool
+from multi_lora_b200.weights import AdapterWeights
+
+pytestmark = pytest.mark.gpu
+
+
+def _weights(modules, rank, keys, seed, dtype=torch.float32):
+    g = torch.Generator().manual_seed(seed)
+    mods = {}
+    for k in keys:
+        n_out, n_in = modules[k]
+        mods[k] = (torch.randn(rank, n_in, generator=g).to(dtype), torch.randn(n_out, rank, generator=g).to(dtype))
+    return AdapterWeights(rank=rank, scaling=1.0 / rank, modules=mods)
+
+
+def test_pool_slots_match_reference_golden(cuda_dev):
+    if not rerun_under_hashseed0("tests/test_pool_gpu.py::test_pool_slots_match_reference_golden"):
+        return
+    g = load_json("pool.json")
+    slots = load_npz("pool_slots.npz")
+    modules = {k: tuple(v) for k, v in g["modules"].items()}
+    for policy, trace in g["traces"].items():
+        pool = LoRAMemoryPool(3, 8, cuda_dev, torch.float32, policy)
+        store = {n: _weights(modules, r, k, s) for n, (r, k, s) in g["specs"].items()}
+        for w in store.values():
+            pool.ensure_buffers(w)
+        for i, step in enumerate(trace):
+            pool.prepare_lora_batch(set(step["names"]), weight_store=store)
+            torch.cuda.synchronize()
+            for k in modules:
+                a, b = pool.get_module_buffers(k)
+                np.testing.assert_array_equal(a.cpu().numpy(), slots[f"{policy}_{i}_{k}_A"], err_msg=f"{policy} {i}")
+                np.testing.assert_array_equal(b.cpu().numpy(), slots[f"{policy}_{i}_{k}_B"], err_msg=f"{policy} {i}")
+        pool.buffers.check_status()
+
+
+MODULES = {"m1": (4, 3), "m2": (5, 3), "big": (1000, 520)}
+
+
+def _check_resident(pool, ref):
+    for name, slot in pool.name_to_slot.items():
+        if name is None:
+            continue
+        w = ref[name]
+        r = w.rank
+        for key in MODULES:
+            a, b = pool.get_slot_weights(slot, key)
+            if key in w.modules:
+                wa, wb = w.modules[key]
+                assert torch.equal(a[:r].cpu(), wa), (name, key)
+                assert torch.equal(b[:, :r].cpu(), wb), (name, key)
+            else:
+                assert a[:r].abs().sum() == 0 and b[:, :r].abs().sum() == 0, (name, key)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_pool_rounds_like_reference_gpu_test(cuda_dev, dtype):
+    specs = {"a": (8, ["m1", "m2", "big"], 1), "b": (8, ["m1"], 2), "c": (4, ["m1", "m2", "big"], 3),
+             "d": (4, ["m2"], 4), "e": (8, ["m1", "m2", "big"], 5), "f": (8, ["m1", "m2"], 6),
+             "g": (8, ["m2", "big"], 7)}
+    store = {n: _weights(MODULES, r, k, s, dtype) for n, (r, k, s) in specs.items()}
+    ref = {n: _weights(MODULES, r, k, s, dtype) for n, (r, k, s) in specs.items()}
+    pool = LoRAMemoryPool(8, 8, cuda_dev, dtype)
+    for w in store.values():
+        pool.ensure_buffers(w)
+    rounds = [{"a", "b", "c", "d"}, {"e"}, {"a", "c", "e"}, {"b", "d"}, {"a", "b", "e", "f", "g"}]
+    assert len(rounds[-1]) > _BANK_CHUNK
+    for names in rounds:
+        pool.prepare_lora_batch(names, weight_store=store)
+        torch.cuda.synchronize()
+        _check_resident(pool, ref)
+    assert len(pool.buffers._banks) <= len(store)
+    assert all(store[n].flattened for n in store)
+    pool.buffers.check_status()
+
+
+def test_load_overlaps_on_copy_stream_and_compute_waits(cuda_dev):
+    """The H2D + scatter run on the pool's copy stream; the compute stream waits on its event."""
+    pool = LoRAMemoryPool(2, 8, cuda_dev, torch.bfloat16)
+    store = {"a": _weights(MODULES, 8, ["big"], 1, torch.bfloat16)}
+    ref = _weights(MODULES, 8, ["big"], 1, torch.bfloat16)
+    pool.ensure_buffers(store["a"])
+    pool.prepare_lora_batch({"a"}, weight_store=store)
+    # no explicit synchronize: a compute-stream read must observe the loaded slot
+    a, _ = pool.get_slot_weights(pool.get_slot_id("a"), "big")
+    first = a[:8].clone()
+    torch.cuda.synchronize()
+    assert torch.equal(first.cpu(), ref.modules["big"][0])
+    assert pool.buffers._copy_stream is not None
