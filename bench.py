@@ -115,9 +115,29 @@ def build_workload(dev, seed: int = 0):
     return layers
 
 
-def run_step(layers, be, parts=("rmsnorm", "lora")):
+def run_step(layers, be, parts=("rmsnorm", "lora"), grouped=True):
+    """One forward of the LoRA hot path over all layers.
+
+    grouped: q/k/v (shared input) and gate/up (shared input) each go through one
+    ``apply_lora_group`` call, which is the dependency structure of the model
+    (rmsnorm -> {q,k,v} -> o -> rmsnorm -> {gate,up} -> down); otherwise every
+    projection is its own ``apply_lora`` call.
+    """
     from multi_lora_b200.rmsnorm import rmsnorm_out
 
+    if grouped and "lora" in parts:
+        for L in layers:
+            if "rmsnorm" in parts:
+                rmsnorm_out(L.h1, L.w1, EPS, L.xn1)
+            qkv = ("q", "k", "v")
+            be.apply_lora_group(L.xn1, [L.A[n] for n in qkv], [L.B[n] for n in qkv], [L.y[n] for n in qkv])
+            be.apply_lora(L.x["o"], L.A["o"], L.B["o"], L.y["o"])
+            if "rmsnorm" in parts:
+                rmsnorm_out(L.h2, L.w2, EPS, L.xn2)
+            gu = ("gate", "up")
+            be.apply_lora_group(L.xn2, [L.A[n] for n in gu], [L.B[n] for n in gu], [L.y[n] for n in gu])
+            be.apply_lora(L.x["down"], L.A["down"], L.B["down"], L.y["down"])
+        return
     for L in layers:
         if "rmsnorm" in parts:
             rmsnorm_out(L.h1, L.w1, EPS, L.xn1)
@@ -288,6 +308,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ungrouped", action="store_true",
+                    help="one apply_lora call per projection instead of grouping q/k/v and gate/up")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -337,8 +359,11 @@ def main() -> None:
     be.set_kernel_input_metadata(meta)
     torch.cuda.synchronize()
 
-    step_graph = capture(lambda: run_step(layers, be))
-    launches_per_step = LAYERS * (2 + 2 * len(LLAMA2_7B))
+    grouped = not args.ungrouped
+    step_graph = capture(lambda: run_step(layers, be, grouped=grouped))
+    fused = _native.capi().mlora_last_apply_path() == 1
+    lora_calls = 4 if grouped else 7
+    launches_per_step = LAYERS * (2 + lora_calls * (1 if fused else 2))
 
     for _ in range(args.warmup):
         step_graph.replay()
@@ -370,30 +395,36 @@ def main() -> None:
         ms = float(t.item())
     value = TOKENS * n / (ms / 1e3)
 
-    # ---- per kernel class: roofline of the dominant one ----
+    # ---- roofline of the dominant kernel (the apply_lora launches), timed alone ----
     ab = algorithmic_bytes(ids)
-    cls_ms = {}
-    for part in ("shrink", "expand", "rmsnorm"):
-        g = capture(lambda p=part: run_step(layers, be, parts=(p,)))
-        cls_ms[part] = time_graph(g, max(20, args.steps // 4))
-        del g
-    n_launch = {"shrink": LAYERS * 7, "expand": LAYERS * 7, "rmsnorm": LAYERS * 2}
-    dom = max(cls_ms, key=cls_ms.get)
     pk = peaks()
-    per_launch_bytes = ab[dom] / n_launch[dom]
-    per_launch_ms = cls_ms[dom] / n_launch[dom]
+    g_lora = capture(lambda: run_step(layers, be, parts=("lora",), grouped=grouped))
+    lora_ms = time_graph(g_lora, max(20, args.steps // 4))
+    del g_lora
+    g_rms = capture(lambda: run_step(layers, be, parts=("rmsnorm",)))
+    rms_ms = time_graph(g_rms, max(20, args.steps // 4))
+    del g_rms
+    lora_launches = LAYERS * lora_calls * (1 if fused else 2)
+    lora_bytes = ab["shrink"] + ab["expand"]
+    per_launch_bytes = lora_bytes / lora_launches
+    per_launch_ms = lora_ms / lora_launches
     achieved = per_launch_bytes / (per_launch_ms / 1e3) / 1e9
-    traffic = read_traffic().get(dom)
-    step_bytes = ab["shrink"] + ab["expand"] + ab["rmsnorm"]
+    kernel = "apply_fused_kernel" if fused else "shrink_kernel+expand_kernel"
+    traffic = read_traffic().get(kernel)
+    step_bytes = lora_bytes + ab["rmsnorm"]
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": traffic, "kernel": dom,
-                "peak_source": pk["src"], "bytes_per_launch": per_launch_bytes,
-                "launch_us": round(per_launch_ms * 1e3, 3)}
+                "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": traffic, "kernel": kernel,
+                "peak_source": pk["src"], "bytes_per_launch": round(per_launch_bytes),
+                "launch_us": round(per_launch_ms * 1e3, 3), "launches_timed": lora_launches}
     step_achieved = step_bytes / (ms / 1e3) / 1e9
     step_roofline = {"bytes_per_step": step_bytes, "achieved": round(step_achieved, 1),
                      "frac": round(step_achieved / pk["hbm_gbs"], 4), "unit": "GB/s",
-                     "class_ms_when_alone": {k: round(v, 4) for k, v in cls_ms.items()},
+                     "lora_ms_alone": round(lora_ms, 4), "rmsnorm_ms_alone": round(rms_ms, 4),
                      "distinct_adapters": ab["distinct_adapters"]}
+    if grouped:  # the same work as one apply_lora call per projection, for comparison
+        g_u = capture(lambda: run_step(layers, be, grouped=False))
+        step_roofline["ungrouped_ms_per_step"] = round(time_graph(g_u, max(20, args.steps // 4)), 4)
+        del g_u
 
     # ---- e2e: public API with host buffers, copies inside the timed region ----
     h_in = torch.randn(TOKENS, HIDDEN).bfloat16().pin_memory()
@@ -434,7 +465,7 @@ def main() -> None:
                "data": "synthetic (seeded; random-init adapters of the named shapes)",
                "config": config_block(n), "roofline": roofline, "step_roofline": step_roofline,
                "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
-               "clocks": clk, "pdl": _native.get_pdl()}
+               "clocks": clk, "pdl": _native.get_pdl(), "grouped": grouped, "fused_path": fused}
         print(json.dumps(out), flush=True)
     del step_graph
     if world > 1:

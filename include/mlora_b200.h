@@ -38,6 +38,7 @@ extern "C" {
 #define MLORA_STATUS_RANK_RANGE 0x2u    /* lora_ranks[s] outside [0, max_rank] (clamped) */
 #define MLORA_STATUS_INDPTR 0x4u        /* seg_indptr decreasing or past the row count */
 #define MLORA_STATUS_SCATTER_RANGE 0x8u /* scatter descriptor outside its buffers */
+#define MLORA_STATUS_TIMEOUT 0x10u      /* a bounded wait for an async copy gave up */
 
 /*
  * Segment routing of one step; mirrors KernelInputMetaData
@@ -110,6 +111,26 @@ int mlora_apply_lora(const void* x, int64_t rows, int64_t in_dim, int64_t x_row_
                      int32_t dtype, uint32_t* status, void* stream);
 
 /*
+ * apply_lora over n (1..4) projections that share x and the routing, e.g.
+ * q/k/v of one attention block or gate/up of one MLP: projection i uses
+ * a_stacks[i] [num_slots, max_rank, in_dim], b_stacks[i]
+ * [num_slots, out_dims[i], max_rank] and updates ys[i] (row stride
+ * y_row_strides[i]) in place, exactly as n separate mlora_apply_lora calls
+ * would. For short segments all n run in one launch. `mid` ([rows, >=
+ * max_rank], may be NULL when the fused path applies) is scratch for the
+ * two-launch path; its contents afterwards are unspecified.
+ * Batches the reference's per-projection LinearWithLoRA.add_delta calls
+ * (multi_lora/layers.py:76-88) the way QKVProjGroup batches the base GEMM
+ * (layers.py:91-125); the reference's kernels reserve a stack_num parameter
+ * for it (kernels/sgemm_lora_a.py:51).
+ */
+int mlora_apply_lora_group(const void* x, int64_t rows, int64_t in_dim, int64_t x_row_stride, int32_t n,
+                           const void* const* a_stacks, const void* const* b_stacks, const int64_t* out_dims,
+                           void* const* ys, const int64_t* y_row_strides, int64_t max_rank,
+                           const mlora_kernel_input_metadata_t* meta, void* mid, int64_t mid_row_stride,
+                           int32_t dtype, uint32_t* status, void* stream);
+
+/*
  * RMSNorm: y[r, :] = dtype( x_f32 * rsqrt(mean(x_f32^2) + eps) * w_f32 ).
  * Row r of x starts at (r / inner) * stride_outer + (r % inner) * stride_inner
  * (elements); y is [rows, hidden] with row stride y_row_stride. w has
@@ -162,6 +183,10 @@ const char* mlora_last_error(void);
 
 /* ABI version: major * 10000 + minor * 100 + patch. */
 int mlora_version(void);
+
+/* Diagnostics: which path the last mlora_apply_lora on this thread took
+ * (1 = one fused launch, 2 = shrink + expand launches, 0 = none yet). */
+int mlora_last_apply_path(void);
 
 #ifdef __cplusplus
 }

@@ -54,6 +54,8 @@ class CudaLoRABackend(LoRABackend):
                 names.append("seg_indptr decreasing or past the row count")
             if bits & 8:
                 names.append("scatter descriptor out of range")
+            if bits & 16:
+                names.append("an asynchronous copy did not complete in time")
             raise RuntimeError("mlora: invalid routing metadata: " + "; ".join(names))
 
     def _meta(self) -> KernelInputMetaData:
@@ -77,6 +79,48 @@ class CudaLoRABackend(LoRABackend):
             x, weights.contiguous(), _i32(meta.seg_lens), _i32(meta.seg_indptr), _i32(meta.weight_indices),
             _i32(meta.lora_ranks), int(meta.bs), int(meta.max_len), out, self.stack_num,
             self.status_word(x.device))
+
+    def apply_lora(
+        self,
+        x: torch.Tensor,
+        a_stack: torch.Tensor,
+        b_stack: torch.Tensor,
+        base_output: torch.Tensor,
+    ) -> torch.Tensor:
+        """Shrink + expand into base_output in place; one fused launch for short segments.
+
+        ``mid_buffer`` still receives the shrink output, as with two launches.
+        """
+        meta = self._meta()
+        x = self._check_x(x, "x")
+        mid = self.mid_buffer(x.shape[0], a_stack.shape[-2], x)
+        out = base_output
+        target = out if (out.dim() == 2 and out.stride(1) == 1) else out.contiguous()
+        self._ops.apply_lora(
+            x, a_stack.contiguous(), b_stack.contiguous(), _i32(meta.seg_lens), _i32(meta.seg_indptr),
+            _i32(meta.weight_indices), _i32(meta.lora_ranks), meta.scalings, int(meta.bs), int(meta.max_len),
+            mid, target, self.status_word(x.device))
+        if target is not out:
+            out.copy_(target)
+        return out
+
+    def apply_lora_group(self, x: torch.Tensor, a_stacks, b_stacks, base_outputs) -> list:
+        """apply_lora for up to 4 projections that share ``x`` and the routing
+        (q/k/v, gate/up): one launch for short segments. Each base output is
+        updated in place and returned."""
+        meta = self._meta()
+        x = self._check_x(x, "x")
+        outs = list(base_outputs)
+        targets = [o if (o.dim() == 2 and o.stride(1) == 1) else o.contiguous() for o in outs]
+        mid = self.mid_buffer(x.shape[0], a_stacks[0].shape[-2], x)
+        self._ops.apply_lora_group(
+            x, [a.contiguous() for a in a_stacks], [b.contiguous() for b in b_stacks], _i32(meta.seg_lens),
+            _i32(meta.seg_indptr), _i32(meta.weight_indices), _i32(meta.lora_ranks), meta.scalings, int(meta.bs),
+            int(meta.max_len), targets, mid, self.status_word(x.device))
+        for o, t in zip(outs, targets):
+            if t is not o:
+                o.copy_(t)
+        return outs
 
     def run_lora_b_sgemm(
         self,

@@ -12,6 +12,7 @@
 namespace {
 
 thread_local char g_err[512] = {0};
+thread_local int g_last_apply_path = 0;  // 1 fused launch, 2 shrink + expand
 int g_pdl = -1;  // -1: not read from the environment yet
 
 int fail(int code, const char* fmt, ...) {
@@ -64,6 +65,7 @@ extern "C" {
 
 const char* mlora_last_error(void) { return g_err; }
 int mlora_version(void) { return 100; }
+int mlora_last_apply_path(void) { return g_last_apply_path; }
 void mlora_set_pdl(int enable) { g_pdl = enable ? 1 : 0; }
 int mlora_get_pdl(void) { return pdl_on() ? 1 : 0; }
 
@@ -160,17 +162,111 @@ int mlora_sgemm_lora_b_fwd(const void* mid, int64_t rows, int64_t mid_row_stride
   return cuda_status(mlora::launch_expand(a, dtype, mid_f32, (cudaStream_t)stream, pdl_on()), "expand launch");
 }
 
+namespace {
+
+// Shared body of mlora_apply_lora / mlora_apply_lora_group: one fused launch
+// over every projection when the shape allows it, else shrink + expand per
+// projection through `mid`. `mids` (optional, per projection) receive the
+// shrink output on the fused path.
+int apply_impl(const void* x, int64_t rows, int64_t in_dim, int64_t x_row_stride, int32_t n,
+               const void* const* a_stacks, const void* const* b_stacks, const int64_t* out_dims,
+               void* const* mids, void* mid, int64_t mid_row_stride, void* const* ys, const int64_t* y_row_strides,
+               int64_t max_rank, const mlora_kernel_input_metadata_t* meta, int32_t dtype, uint32_t* status,
+               void* stream) {
+  g_err[0] = 0;
+  if (int rc = check_meta(meta, rows)) return rc;
+  const int es = elem_size(dtype);
+  if (es == 0) return fail(MLORA_ERR_UNSUPPORTED_DTYPE, "unsupported dtype code %d", dtype);
+  if (n < 1 || n > mlora::kMaxFusedModules)
+    return fail(MLORA_ERR_INVALID_ARGUMENT, "projection count %d outside [1, %d]", n, mlora::kMaxFusedModules);
+  if (in_dim <= 0 || in_dim > INT32_MAX) return fail(MLORA_ERR_INVALID_ARGUMENT, "in_dim %lld invalid", (long long)in_dim);
+  if (max_rank <= 0 || max_rank > 65535) return fail(MLORA_ERR_INVALID_ARGUMENT, "max_rank %lld invalid", (long long)max_rank);
+  if (x_row_stride < in_dim) return fail(MLORA_ERR_INVALID_ARGUMENT, "x_row_stride < in_dim");
+  if (a_stacks == nullptr || b_stacks == nullptr || out_dims == nullptr || ys == nullptr || y_row_strides == nullptr)
+    return fail(MLORA_ERR_INVALID_ARGUMENT, "projection arrays are NULL");
+  for (int i = 0; i < n; ++i) {
+    if (out_dims[i] <= 0 || out_dims[i] > INT32_MAX)
+      return fail(MLORA_ERR_INVALID_ARGUMENT, "out_dim[%d] %lld invalid", i, (long long)out_dims[i]);
+    if (y_row_strides[i] < out_dims[i]) return fail(MLORA_ERR_INVALID_ARGUMENT, "y_row_stride[%d] < out_dim", i);
+  }
+  if (meta->bs == 0 || rows == 0) return MLORA_OK;
+  if (meta->scalings == nullptr) return fail(MLORA_ERR_INVALID_ARGUMENT, "scalings is NULL");
+  if (elem_size(meta->scalings_dtype) == 0)
+    return fail(MLORA_ERR_UNSUPPORTED_DTYPE, "unsupported scalings dtype %d", meta->scalings_dtype);
+  bool fusable = es == 2 && meta->max_len <= 16 && rows <= 64LL * meta->num_slots && x != nullptr &&
+                 x_row_stride % 8 == 0 && aligned(x, 16);
+  for (int i = 0; i < n && fusable; ++i)
+    fusable = a_stacks[i] != nullptr && b_stacks[i] != nullptr && ys[i] != nullptr && aligned(a_stacks[i], 16) &&
+              aligned(b_stacks[i], 16) && (mids == nullptr || mids[i] == nullptr || mid_row_stride >= max_rank);
+  if (fusable) {
+    mlora::FusedArgs f{};
+    f.x = x;
+    f.x_stride = x_row_stride;
+    f.n_mod = n;
+    for (int i = 0; i < n; ++i) {
+      mlora::FusedModule& m = f.mod[i];
+      m.a = a_stacks[i];
+      m.b = b_stacks[i];
+      m.y = ys[i];
+      m.y_stride = y_row_strides[i];
+      m.mid = mids != nullptr ? mids[i] : nullptr;
+      m.mid_stride = mid_row_stride;
+      m.out_dim = (int)out_dims[i];
+    }
+    f.seg_indptr = meta->seg_indptr;
+    f.weight_indices = meta->weight_indices;
+    f.lora_ranks = meta->lora_ranks;
+    f.scalings = meta->scalings;
+    f.scalings_dtype = meta->scalings_dtype;
+    f.bs = meta->bs;
+    f.S = (int)rows;
+    f.in_dim = (int)in_dim;
+    f.R = (int)max_rank;
+    f.num_slots = meta->num_slots;
+    f.status = status;
+    const cudaError_t e = mlora::launch_apply_fused(f, dtype, (cudaStream_t)stream, pdl_on());
+    if (e == cudaSuccess) {
+      g_last_apply_path = 1;
+      return MLORA_OK;
+    }
+    if (e != cudaErrorNotSupported) return cuda_status(e, "fused apply_lora launch");
+  }
+  g_last_apply_path = 2;
+  if (mid == nullptr) return fail(MLORA_ERR_INVALID_ARGUMENT, "mid buffer required for this shape");
+  for (int i = 0; i < n; ++i) {
+    int rc = mlora_sgemm_lora_a_fwd(x, rows, in_dim, x_row_stride, a_stacks[i], max_rank, meta, mid, mid_row_stride,
+                                    dtype, dtype, 1, status, stream);
+    if (rc != MLORA_OK) return rc;
+    rc = mlora_sgemm_lora_b_fwd(mid, rows, mid_row_stride, dtype, b_stacks[i], out_dims[i], max_rank, meta, ys[i],
+                                y_row_strides[i], dtype, status, stream);
+    if (rc != MLORA_OK) return rc;
+  }
+  return MLORA_OK;
+}
+
+}  // namespace
+
 int mlora_apply_lora(const void* x, int64_t rows, int64_t in_dim, int64_t x_row_stride,
                      const void* a_stack, const void* b_stack, int64_t out_dim, int64_t max_rank,
                      const mlora_kernel_input_metadata_t* meta,
                      void* mid, int64_t mid_row_stride,
                      void* y, int64_t y_row_stride,
                      int32_t dtype, uint32_t* status, void* stream) {
-  int rc = mlora_sgemm_lora_a_fwd(x, rows, in_dim, x_row_stride, a_stack, max_rank, meta, mid, mid_row_stride,
-                                  dtype, dtype, 1, status, stream);
-  if (rc != MLORA_OK) return rc;
-  return mlora_sgemm_lora_b_fwd(mid, rows, mid_row_stride, dtype, b_stack, out_dim, max_rank, meta, y,
-                                y_row_stride, dtype, status, stream);
+  void* const mids[1] = {mid};
+  void* const ys[1] = {y};
+  const int64_t y_strides[1] = {y_row_stride};
+  const int64_t outs[1] = {out_dim};
+  return apply_impl(x, rows, in_dim, x_row_stride, 1, &a_stack, &b_stack, outs, mids, mid, mid_row_stride, ys,
+                    y_strides, max_rank, meta, dtype, status, stream);
+}
+
+int mlora_apply_lora_group(const void* x, int64_t rows, int64_t in_dim, int64_t x_row_stride, int32_t n,
+                           const void* const* a_stacks, const void* const* b_stacks, const int64_t* out_dims,
+                           void* const* ys, const int64_t* y_row_strides, int64_t max_rank,
+                           const mlora_kernel_input_metadata_t* meta, void* mid, int64_t mid_row_stride,
+                           int32_t dtype, uint32_t* status, void* stream) {
+  return apply_impl(x, rows, in_dim, x_row_stride, n, a_stacks, b_stacks, out_dims, nullptr, mid, mid_row_stride, ys,
+                    y_row_strides, max_rank, meta, dtype, status, stream);
 }
 
 int mlora_rmsnorm_fwd(const void* x, int64_t rows, int64_t hidden, int64_t stride_outer,

@@ -60,6 +60,38 @@ struct RmsNormArgs {
   int vec_ok;
 };
 
+// One projection of a fused apply_lora launch; up to kMaxFusedModules
+// projections that share x and the routing go in one launch (e.g. q/k/v).
+constexpr int kMaxFusedModules = 4;
+struct FusedModule {
+  const void* a;          // A stack [K, R, in], contiguous
+  const void* b;          // B stack [K, out, R], contiguous
+  void* y;                // [S, out] at y_stride, updated in place
+  void* mid;              // optional [S, >= R] at mid_stride (shrink output, as the API returns it)
+  int64_t y_stride;
+  int64_t mid_stride;
+  int out_dim;
+  int ob;                 // output columns per cluster CTA (multiple of 8), set by the launcher
+  int y_tma;              // y rows may be staged with bulk copies (alignment holds)
+};
+
+struct FusedArgs {
+  const void* x;          // [S, in] rows at x_stride elements
+  int64_t x_stride;
+  FusedModule mod[kMaxFusedModules];
+  int n_mod;
+  const int32_t* seg_indptr;
+  const int32_t* weight_indices;
+  const int32_t* lora_ranks;
+  const void* scalings;
+  int scalings_dtype;
+  int bs, S, in_dim, R, num_slots;
+  int ks;                 // input columns per cluster CTA (multiple of 8), set by the launcher
+  int ob_max;             // largest module ob (sizes the shared-memory B and y tiles)
+  uint32_t* status;
+};
+
+cudaError_t launch_apply_fused(FusedArgs a, int dtype, cudaStream_t st, bool pdl);
 cudaError_t launch_shrink(const ShrinkArgs& a, int dtype, bool out_f32, cudaStream_t st, bool pdl);
 cudaError_t launch_expand(const ExpandArgs& a, int dtype, bool mid_f32, cudaStream_t st, bool pdl);
 cudaError_t launch_rmsnorm(const RmsNormArgs& a, int dtype, cudaStream_t st, bool pdl);

@@ -9,6 +9,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/library.h>
 
+#include <vector>
+
 #include "../../include/mlora_b200.h"
 
 namespace {
@@ -124,6 +126,100 @@ at::Tensor sgemm_lora_b(const at::Tensor& x, const at::Tensor& weights, const at
   return output;
 }
 
+// apply_lora (backend/base.py:60-89): shrink into `mid`, expand into `output`
+// in place; one fused launch for short segments.
+at::Tensor apply_lora(const at::Tensor& x, const at::Tensor& a_stack, const at::Tensor& b_stack,
+                      const at::Tensor& seg_lens, const at::Tensor& seg_indptr, const at::Tensor& weight_indices,
+                      const at::Tensor& lora_ranks, const at::Tensor& scalings, int64_t bs, int64_t max_len,
+                      at::Tensor mid, at::Tensor output, const c10::optional<at::Tensor>& status) {
+  const at::Device dev = x.device();
+  check_cuda(x, "x", dev);
+  check_cuda(a_stack, "a_stack", dev);
+  check_cuda(b_stack, "b_stack", dev);
+  check_cuda(mid, "mid", dev);
+  check_cuda(output, "output", dev);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "mlora: x must be [S, in] with unit column stride");
+  TORCH_CHECK(a_stack.dim() == 3 && a_stack.is_contiguous(), "mlora: a_stack must be contiguous [K, max_rank, in]");
+  TORCH_CHECK(b_stack.dim() == 3 && b_stack.is_contiguous(), "mlora: b_stack must be contiguous [K, out, max_rank]");
+  TORCH_CHECK(a_stack.size(2) == x.size(1), "mlora: a_stack in_dim ", a_stack.size(2), " != x in_dim ", x.size(1));
+  TORCH_CHECK(a_stack.size(0) == b_stack.size(0) && a_stack.size(1) == b_stack.size(2),
+              "mlora: a_stack ", a_stack.sizes(), " and b_stack ", b_stack.sizes(), " disagree");
+  TORCH_CHECK(a_stack.scalar_type() == x.scalar_type() && b_stack.scalar_type() == x.scalar_type() &&
+                  output.scalar_type() == x.scalar_type() && mid.scalar_type() == x.scalar_type(),
+              "mlora: x, stacks, mid and output must share one dtype");
+  TORCH_CHECK(mid.dim() == 2 && mid.stride(1) == 1 && mid.size(0) >= x.size(0) && mid.size(1) >= a_stack.size(1),
+              "mlora: mid must be [>= S, >= max_rank] with unit column stride");
+  TORCH_CHECK(output.dim() == 2 && output.stride(1) == 1 && output.size(0) == x.size(0) &&
+                  output.size(1) == b_stack.size(1),
+              "mlora: output must be [S, out] with unit column stride");
+  TORCH_CHECK(lora_ranks.numel() == a_stack.size(0), "mlora: lora_ranks length != number of slots");
+  const c10::cuda::CUDAGuard guard(dev);
+  const auto meta = make_meta(seg_lens, seg_indptr, weight_indices, lora_ranks, &scalings, bs, max_len, dev);
+  const int rc = mlora_apply_lora(x.data_ptr(), x.size(0), x.size(1), x.stride(0), a_stack.data_ptr(),
+                                  b_stack.data_ptr(), b_stack.size(1), a_stack.size(1), &meta, mid.data_ptr(),
+                                  mid.stride(0), output.data_ptr(), output.stride(0), dt_code(x.scalar_type()),
+                                  status_ptr(status, dev), at::cuda::getCurrentCUDAStream().stream());
+  check_rc(rc);
+  return output;
+}
+
+// apply_lora over projections sharing x and the routing (q/k/v, gate/up).
+void apply_lora_group(const at::Tensor& x, at::TensorList a_stacks, at::TensorList b_stacks,
+                      const at::Tensor& seg_lens, const at::Tensor& seg_indptr, const at::Tensor& weight_indices,
+                      const at::Tensor& lora_ranks, const at::Tensor& scalings, int64_t bs, int64_t max_len,
+                      at::TensorList outputs, const c10::optional<at::Tensor>& mid,
+                      const c10::optional<at::Tensor>& status) {
+  const at::Device dev = x.device();
+  check_cuda(x, "x", dev);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "mlora: x must be [S, in] with unit column stride");
+  const int64_t n = (int64_t)a_stacks.size();
+  TORCH_CHECK(n >= 1 && n <= 4 && (int64_t)b_stacks.size() == n && (int64_t)outputs.size() == n,
+              "mlora: 1..4 projections with one a_stack, b_stack and output each");
+  std::vector<const void*> a(n), b(n);
+  std::vector<void*> y(n);
+  std::vector<int64_t> outs(n), ystr(n);
+  const int64_t R = a_stacks[0].size(1);
+  for (int64_t i = 0; i < n; ++i) {
+    check_cuda(a_stacks[i], "a_stack", dev);
+    check_cuda(b_stacks[i], "b_stack", dev);
+    check_cuda(outputs[i], "output", dev);
+    TORCH_CHECK(a_stacks[i].dim() == 3 && a_stacks[i].is_contiguous() && a_stacks[i].size(2) == x.size(1) &&
+                    a_stacks[i].size(1) == R && a_stacks[i].size(0) == lora_ranks.numel(),
+                "mlora: a_stack ", i, " must be contiguous [K, max_rank, in]");
+    TORCH_CHECK(b_stacks[i].dim() == 3 && b_stacks[i].is_contiguous() && b_stacks[i].size(2) == R &&
+                    b_stacks[i].size(0) == lora_ranks.numel(),
+                "mlora: b_stack ", i, " must be contiguous [K, out, max_rank]");
+    TORCH_CHECK(outputs[i].dim() == 2 && outputs[i].stride(1) == 1 && outputs[i].size(0) == x.size(0) &&
+                    outputs[i].size(1) == b_stacks[i].size(1),
+                "mlora: output ", i, " must be [S, out] with unit column stride");
+    TORCH_CHECK(a_stacks[i].scalar_type() == x.scalar_type() && b_stacks[i].scalar_type() == x.scalar_type() &&
+                    outputs[i].scalar_type() == x.scalar_type(),
+                "mlora: x, stacks and outputs must share one dtype");
+    a[i] = a_stacks[i].data_ptr();
+    b[i] = b_stacks[i].data_ptr();
+    y[i] = outputs[i].data_ptr();
+    outs[i] = b_stacks[i].size(1);
+    ystr[i] = outputs[i].stride(0);
+  }
+  void* mid_ptr = nullptr;
+  int64_t mid_stride = R;
+  if (mid.has_value()) {
+    check_cuda(*mid, "mid", dev);
+    TORCH_CHECK(mid->dim() == 2 && mid->stride(1) == 1 && mid->size(0) >= x.size(0) && mid->size(1) >= R &&
+                    mid->scalar_type() == x.scalar_type(),
+                "mlora: mid must be [>= S, >= max_rank] like x");
+    mid_ptr = mid->data_ptr();
+    mid_stride = mid->stride(0);
+  }
+  const c10::cuda::CUDAGuard guard(dev);
+  const auto meta = make_meta(seg_lens, seg_indptr, weight_indices, lora_ranks, &scalings, bs, max_len, dev);
+  const int rc = mlora_apply_lora_group(x.data_ptr(), x.size(0), x.size(1), x.stride(0), (int32_t)n, a.data(),
+                                        b.data(), outs.data(), y.data(), ystr.data(), R, &meta, mid_ptr, mid_stride,
+                                        dt_code(x.scalar_type()), status_ptr(status, dev),
+                                        at::cuda::getCurrentCUDAStream().stream());
+  check_rc(rc);
+}
+
 // Two-level row addressing of the reference (kernels/rmsnorm.py:59-81).
 void rms_layout(const at::Tensor& x, int64_t hidden, int64_t rows, int64_t& so, int64_t& si, int64_t& inner,
                 at::Tensor& src) {
@@ -183,6 +279,14 @@ TORCH_LIBRARY(mlora, m) {
       "sgemm_lora_b(Tensor x, Tensor weights, Tensor seg_lens, Tensor seg_indptr, Tensor weight_indices, "
       "Tensor lora_ranks, Tensor scalings, int bs, int max_len, Tensor(a!) output, Tensor(b!)? status=None) "
       "-> Tensor(a!)");
+  m.def(
+      "apply_lora(Tensor x, Tensor a_stack, Tensor b_stack, Tensor seg_lens, Tensor seg_indptr, "
+      "Tensor weight_indices, Tensor lora_ranks, Tensor scalings, int bs, int max_len, Tensor(a!) mid, "
+      "Tensor(b!) output, Tensor(c!)? status=None) -> Tensor(b!)");
+  m.def(
+      "apply_lora_group(Tensor x, Tensor[] a_stacks, Tensor[] b_stacks, Tensor seg_lens, Tensor seg_indptr, "
+      "Tensor weight_indices, Tensor lora_ranks, Tensor scalings, int bs, int max_len, Tensor(a!)[] outputs, "
+      "Tensor(b!)? mid=None, Tensor(c!)? status=None) -> ()");
   m.def("rmsnorm(Tensor x, Tensor weight, float eps) -> Tensor");
   m.def("rmsnorm_out(Tensor x, Tensor weight, float eps, Tensor(a!) out) -> Tensor(a!)");
 }
@@ -190,6 +294,8 @@ TORCH_LIBRARY(mlora, m) {
 TORCH_LIBRARY_IMPL(mlora, CUDA, m) {
   m.impl("sgemm_lora_a", &sgemm_lora_a);
   m.impl("sgemm_lora_b", &sgemm_lora_b);
+  m.impl("apply_lora", &apply_lora);
+  m.impl("apply_lora_group", &apply_lora_group);
   m.impl("rmsnorm", &rmsnorm);
   m.impl("rmsnorm_out", &rmsnorm_out);
 }

@@ -145,6 +145,134 @@ def test_random_cases_match_oracle(cuda_dev, dtype, shape):
     _check_case(c, cuda_dev, dtype)
 
 
+def _check_apply(c, dev, dtype, expect_path=None):
+    """apply_lora through the C ABI (fused launch when eligible) against the oracle."""
+    S = c["x"].shape[0]
+    R = c["A"].shape[1]
+    n_out = c["B"].shape[1]
+    meta = C.make_meta(c["lens"], c["widx"], c["ranks"], c["scal"], dev)
+    mid_big = torch.full((S, R + 8), -3.0, dtype=dtype, device=dev)
+    mid = mid_big[:, :R]
+    p0, p1 = c["pad"]
+    y = c["big"][p0:p0 + S, p1:p1 + n_out]
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    C.check(C.apply_lora(c["x"], c["A"], c["B"], meta, mid, y, status=status))
+    path = _native.capi().mlora_last_apply_path()
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    if expect_path is not None:
+        assert path == expect_path
+    ind = meta.seg_indptr.cpu().numpy()
+    want = O.apply_lora_fp32(C.f32(c["x"]), np.nan_to_num(C.f32(c["A"])), np.nan_to_num(C.f32(c["B"])), ind,
+                             c["widx"], c["ranks"], c["scal"], len(c["lens"]), C.f32(c["ybase"]))
+    got = C.f32(y)
+    assert np.isfinite(got).all()
+    np.testing.assert_allclose(got, want, rtol=RTOL, atol=ATOL)
+    big = C.f32(c["big"])
+    inner = np.zeros(big.shape, bool)
+    inner[p0:p0 + S, p1:p1 + n_out] = True
+    assert (big[~inner] == 7.0).all()
+    m = C.f32(mid_big)
+    assert (m[:, R:] == -3.0).all()
+    for seg, slot in enumerate(c["widx"]):
+        r = c["ranks"][slot]
+        rows = slice(ind[seg], ind[seg + 1])
+        assert (m[rows, r:R] == -3.0).all()
+        mid_want = C.f32(c["x"])[rows] @ np.nan_to_num(C.f32(c["A"]))[slot, :r].T
+        np.testing.assert_allclose(m[rows, :r], mid_want, rtol=1e-2, atol=1e-2)
+    return path
+
+
+FUSED_SHAPES = [s for s in SHAPES if s[0] % 8 == 0 and s[2] % 8 == 0 and s[2] <= 64 and max(s[4]) <= 16]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", FUSED_SHAPES, ids=lambda s: f"{s[0]}x{s[1]}r{s[2]}")
+def test_fused_apply_matches_oracle(cuda_dev, dtype, shape):
+    n_in, n_out, R, ranks, lens = shape
+    c = _case(hash((n_in, n_out, R, 1)) % 1000, dtype, n_in, n_out, R, ranks, lens, cuda_dev)
+    _check_apply(c, cuda_dev, dtype, expect_path=1)
+
+
+@pytest.mark.parametrize("shape", [s for s in SHAPES if s not in FUSED_SHAPES], ids=lambda s: f"{s[0]}x{s[1]}r{s[2]}")
+def test_apply_falls_back_to_two_launches(cuda_dev, shape):
+    n_in, n_out, R, ranks, lens = shape
+    c = _case(hash((n_in, n_out, R, 2)) % 1000, torch.bfloat16, n_in, n_out, R, ranks, lens, cuda_dev)
+    _check_apply(c, cuda_dev, torch.bfloat16, expect_path=2)
+
+
+def test_fused_apply_many_segments_and_cluster16(cuda_dev):
+    """bs above one scan pass (256) and an in-dim that needs 16-CTA clusters."""
+    c = _case(21, torch.bfloat16, 512, 640, 16, [16, 16, 8] * 4, [1] * 700, cuda_dev)
+    _check_apply(c, cuda_dev, torch.bfloat16, expect_path=1)
+    c = _case(22, torch.bfloat16, 40960, 1024, 16, [16] * 4, [1] * 16, cuda_dev)
+    _check_apply(c, cuda_dev, torch.bfloat16, expect_path=1)
+
+
+def test_fused_apply_rank0_and_unused_slots_leave_y(cuda_dev):
+    """Only base-model (rank 0) segments: y is bit-identical afterwards."""
+    c = _case(23, torch.bfloat16, 1024, 512, 16, [0, 16, 16], [1] * 8, cuda_dev, nan_tails=False)
+    c["widx"] = [0] * 8
+    before = c["big"].clone()
+    meta = C.make_meta(c["lens"], c["widx"], c["ranks"], c["scal"], cuda_dev)
+    mid = torch.zeros(8, 16, dtype=torch.bfloat16, device=cuda_dev)
+    p0, p1 = c["pad"]
+    C.check(C.apply_lora(c["x"], c["A"], c["B"], meta, mid, c["big"][p0:p0 + 8, p1:p1 + 512]))
+    torch.cuda.synchronize()
+    assert torch.equal(c["big"], before)
+
+
+@pytest.mark.parametrize("outs, R, ranks, lens, path", [
+    ((4096, 1024, 1024), 16, [16] * 8, [1] * 32, 1),        # q/k/v of a GQA block
+    ((11008, 11008), 16, [16, 0, 16, 8], [1] * 24, 1),      # gate/up
+    ((384, 200, 72), 64, [64, 8, 17], [3, 1, 5, 2], 1),     # mixed ranks, out % 8 != 0 for two
+    ((96, 64), 20, [20, 4], [2, 1, 3], 2),                  # R % 8 != 0: two launches per projection
+])
+def test_group_matches_separate_projections(cuda_dev, outs, R, ranks, lens, path):
+    """mlora_apply_lora_group == one oracle apply per projection (shared x and routing)."""
+    import ctypes
+
+    dev, dt = cuda_dev, torch.bfloat16
+    g = torch.Generator().manual_seed(len(outs) * 7 + R)
+    n_in = 256 if R != 20 else 96
+    K = len(ranks)
+    S = sum(lens)
+    widx = torch.randint(0, K, (len(lens),), generator=g).tolist()
+    scal = [0.5 + i for i in range(K)]
+    x = torch.randn(S, n_in, generator=g).to(dt)
+    meta = C.make_meta(lens, widx, ranks, scal, dev)
+    As, Bs, ys, y0 = [], [], [], []
+    for o in outs:
+        a = (torch.randn(K, R, n_in, generator=g) * n_in ** -0.5).to(dt)
+        b = (torch.randn(K, o, R, generator=g) * 0.05).to(dt)
+        for s, r in enumerate(ranks):
+            a[s, r:] = float("nan")
+            b[s, :, r:] = float("nan")
+        yb = torch.randn(S, o, generator=g).to(dt)
+        As.append(a.to(dev))
+        Bs.append(b.to(dev))
+        y0.append(yb)
+        ys.append(yb.to(dev).clone())
+    xd = x.to(dev)
+    mid = torch.zeros(S, R, dtype=dt, device=dev)
+    n = len(outs)
+    P = ctypes.c_void_p
+    arr = lambda vals, t: (t * n)(*vals)  # noqa: E731
+    m = meta.struct()
+    rc = _native.capi().mlora_apply_lora_group(
+        xd.data_ptr(), S, n_in, n_in, n, arr([a.data_ptr() for a in As], P), arr([b.data_ptr() for b in Bs], P),
+        arr(list(outs), ctypes.c_int64), arr([y.data_ptr() for y in ys], P), arr([y.stride(0) for y in ys], ctypes.c_int64),
+        R, ctypes.byref(m), mid.data_ptr(), R, 0, None, torch.cuda.current_stream().cuda_stream)
+    C.check(rc)
+    assert _native.capi().mlora_last_apply_path() == path
+    torch.cuda.synchronize()
+    ind = meta.seg_indptr.cpu().numpy()
+    for a, b, yb, y in zip(As, Bs, y0, ys):
+        want = O.apply_lora_fp32(C.f32(x), np.nan_to_num(C.f32(a)), np.nan_to_num(C.f32(b)), ind, widx, ranks, scal,
+                                 len(lens), C.f32(yb))
+        np.testing.assert_allclose(C.f32(y), want, rtol=RTOL, atol=ATOL)
+
+
 def test_many_segments_more_than_one_pass(cuda_dev):
     """bs above the per-pass segment capacity (256) for one slot."""
     lens = [1] * 700
