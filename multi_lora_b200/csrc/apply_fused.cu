@@ -15,23 +15,29 @@
 //      griddepcontrol.wait, so under programmatic dependent launch the weight
 //      stream overlaps the previous kernel;
 //   2. after the wait it bulk-copies the slot's x rows (its slice) and y rows
-//      (its output block) and computes split-K partials of mid;
+//      (its output block) and computes split-K partials of mid with warp-level
+//      tensor-core tiles (mma.sync m16n8k16: up to 8 tokens per tile cost the
+//      same as one, where a scalar loop would grow with the token count);
 //   3. pushes its partials into every peer CTA's shared memory with st.async
 //      (distributed shared memory; each receiver's mbarrier counts the bytes),
 //      so no cluster-wide barrier sits on the critical path; each CTA sums the
 //      CS partials in a fixed order (deterministic) and rounds to T once, as
 //      the reference stores mid in x's dtype;
-//   4. adds the scaled delta of its output block into y.
+//   4. computes the delta of its output block with the same tensor-core tiles
+//      (A operand = mid rounded to T, exactly what the reference multiplies)
+//      and adds it, scaled, into y.
 // Each slot's A and B are read from HBM exactly once per launch. No global
 // scratch, no atomics. Every wait is bounded (status bit on timeout).
 #include <cooperative_groups.h>
 
 #include <map>
 #include <mutex>
+#include <cstdlib>
 #include <utility>
 
 #include "common.cuh"
 #include "kernels.h"
+#include "mma.cuh"
 #include "tma.cuh"
 
 namespace cg = cooperative_groups;
@@ -115,19 +121,22 @@ __device__ __forceinline__ int fused_token_row(const FusedSegs& sl, int q) {
   return sl.start[lo] + (q - sl.cum[lo]);
 }
 
-// RM: rank rows covered by the shrink thread grid (16, 32 or 64; >= R);
-// KG = NT / RM threads per rank row.
+// Shared-memory row stride (elements) for a row of `k` elements that
+// ldmatrix reads conflict-free: an odd number of 16-byte units.
+__host__ __device__ __forceinline__ int padded_row(int k) { return ((k / 8) % 2 == 0) ? k + 8 : k; }
+
+// RM: rank columns covered by the tiles (16, 32 or 64; >= R).
 template <typename T, int RM>
 __global__ void __launch_bounds__(kFusedNT) apply_fused_kernel(const FusedArgs p) {
   constexpr int NT = kFusedNT;
-  constexpr int V = 8;            // elements per 16-byte chunk (bf16/f16)
-  constexpr int KG = NT / RM;     // threads per rank row in the shrink
-  constexpr int TT = kFusedTT;
+  constexpr int NW = NT / 32;
+  constexpr int TT = kFusedTT;    // tokens per tile (MMA rows 8..15 repeat row 0 and are discarded)
   constexpr int Q4 = RM / 4;      // 16-byte pieces per partial row
+  constexpr int MP = RM + 8;      // padded row of the bf16/f16 mid tile
   __shared__ FusedSegs sl;
   __shared__ int s_rows[TT];
   __shared__ __align__(16) float s_part[TT][RM];
-  __shared__ __align__(16) float s_mid[TT][RM];
+  __shared__ __align__(16) T s_mid[16][MP];
   __shared__ __align__(8) uint64_t bar_w, bar_x, bar_p;
   extern __shared__ __align__(128) unsigned char s_dyn[];
 
@@ -136,41 +145,55 @@ __global__ void __launch_bounds__(kFusedNT) apply_fused_kernel(const FusedArgs p
   const int j = (int)cluster.block_rank();
   const int slot = blockIdx.y;
   const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
   const int R = p.R;
   FusedModule m = p.mod[0];
 #pragma unroll
   for (int i = 1; i < kMaxFusedModules; ++i)
     if (i == (int)blockIdx.z) m = p.mod[i];
 
-  int rank = __ldg(p.lora_ranks + slot);
+  // one memory round trip: warp 0 scans the routing while warp 1 reads rank and scaling
+  __shared__ int s_rank;
+  __shared__ float s_scale;
+  if (tid == 32) {
+    s_rank = __ldg(p.lora_ranks + slot);
+    switch (p.scalings_dtype) {
+      case kBF16: s_scale = __bfloat162float(__ldg(static_cast<const __nv_bfloat16*>(p.scalings) + slot)); break;
+      case kF16: s_scale = __half2float(__ldg(static_cast<const __half*>(p.scalings) + slot)); break;
+      default: s_scale = __ldg(static_cast<const float*>(p.scalings) + slot); break;
+    }
+  }
+  fused_scan(sl, slot, 0, p);
+  __syncthreads();
+  int rank = s_rank;
+  const float scale = s_scale;
   if (rank < 0 || rank > R) {
     if (j == 0 && tid == 0 && blockIdx.z == 0) flag_error(p.status, kErrRankRange);
     rank = rank < 0 ? 0 : R;
   }
-  if (rank == 0) {  // base model: no delta, mid untouched (uniform per cluster)
-    pdl_trigger();
-    return;
-  }
-  fused_scan(sl, slot, 0, p);
-  __syncthreads();
-  if (sl.n == 0 && p.bs <= kFusedScan) {  // slot unused by this batch (uniform per cluster)
+  // base model (rank 0: no delta, mid untouched) or a slot this batch does not
+  // use: the whole cluster leaves (uniform per cluster)
+  if (rank == 0 || (sl.n == 0 && p.bs <= kFusedScan)) {
     pdl_trigger();
     return;
   }
 
-  // shared memory: A [R][ks] | B [ob_max][R] | x [TT][ks] | y [TT][ob_max] | partials in [cs][TT][RM]
-  const int k0 = j * p.ks;                       // multiple of V
+  // shared memory: A [R][kp] | B [ob_max][R] | x [TT][kp] | y [TT][ob_max] |
+  //                warp partials [NW][TT][RM] f32 | partials in [cs][TT][RM] f32
+  const int kp = padded_row(p.ks);
+  const int k0 = j * p.ks;                       // multiple of 16
   const int kend = min(p.in_dim, k0 + p.ks);
-  const int klen = kend > k0 ? kend - k0 : 0;    // multiple of V
-  const int c_end = klen / V;
+  const int klen = kend > k0 ? kend - k0 : 0;    // multiple of 8
+  const int ksteps = (klen + 15) / 16;
   const int o_lo = min(m.out_dim, j * m.ob);
   const int o_hi = min(m.out_dim, o_lo + m.ob);
   const int olen = o_hi - o_lo;
   T* s_a = reinterpret_cast<T*>(s_dyn);
-  T* s_b = s_a + (size_t)R * p.ks;
+  T* s_b = s_a + (size_t)R * kp;
   T* s_x = s_b + (size_t)p.ob_max * R;
-  T* s_y = s_x + (size_t)TT * p.ks;
-  float* s_recv = reinterpret_cast<float*>(s_y + (size_t)TT * p.ob_max);
+  T* s_y = s_x + (size_t)TT * kp;
+  float* s_wred = reinterpret_cast<float*>(s_y + (size_t)TT * p.ob_max);
+  float* s_recv = s_wred + (size_t)NW * TT * RM;
 
   // ---- prologue: adapter weights (stable for the step) into shared memory ----
   if (tid == 0) {
@@ -179,6 +202,9 @@ __global__ void __launch_bounds__(kFusedNT) apply_fused_kernel(const FusedArgs p
     mbar_init(&bar_p, 1);
     fence_barrier_init();
   }
+  for (int e = tid; e < 16 * MP; e += NT) (&s_mid[0][0])[e] = Num<T>::from_f(0.f);
+  if (klen % 16 != 0)  // half k-step at the slice end: zero the 8 pad columns of the rank rows
+    for (int e = tid; e < rank * 8; e += NT) s_a[(size_t)(e / 8) * kp + klen + (e % 8)] = Num<T>::from_f(0.f);
   __syncthreads();
   cluster_arrive_release();  // this CTA runs and its barriers exist; peers wait before pushing to it
   const T* __restrict__ a_src = static_cast<const T*>(m.a) + (int64_t)slot * R * p.in_dim + k0;
@@ -190,31 +216,27 @@ __global__ void __launch_bounds__(kFusedNT) apply_fused_kernel(const FusedArgs p
     mbar_arrive_expect_tx(&bar_w, a_bytes + b_bytes);
     if (klen > 0)
       for (int n = 0; n < rank; ++n)
-        bulk_copy_g2s(s_a + (size_t)n * p.ks, a_src + (int64_t)n * p.in_dim, klen * sizeof(T), &bar_w);
+        bulk_copy_g2s(s_a + (size_t)n * kp, a_src + (int64_t)n * p.in_dim, klen * sizeof(T), &bar_w);
     if (b_bytes > 0) bulk_copy_g2s(s_b, b_src, b_bytes, &bar_w);
   }
-  const int rc = (rank + V - 1) / V;  // B chunks per row that hold rank columns
+  const int rc = (rank + 7) / 8;  // 16-byte B chunks per row that hold rank columns
   if (!b_dense) {  // rows of R with only `rank` valid columns: 16-byte copies per thread
     for (int e = tid; e < olen * rc; e += NT) {
       const int row = e / rc, c = e - row * rc;
-      cp_async16(s_b + (size_t)row * R + c * V, b_src + (int64_t)row * R + c * V);
+      cp_async16(s_b + (size_t)row * R + c * 8, b_src + (int64_t)row * R + c * 8);
     }
-  }
-  float scale;
-  switch (p.scalings_dtype) {
-    case kBF16: scale = __bfloat162float(__ldg(static_cast<const __nv_bfloat16*>(p.scalings) + slot)); break;
-    case kF16: scale = __half2float(__ldg(static_cast<const __half*>(p.scalings) + slot)); break;
-    default: scale = __ldg(static_cast<const float*>(p.scalings) + slot); break;
   }
   pdl_trigger();
   pdl_wait();  // x and y come from earlier kernels
 
   const T* __restrict__ xbase = static_cast<const T*>(p.x);
   T* __restrict__ ybase = static_cast<T*>(m.y);
+  const uint32_t sa_addr = smem_addr(s_a), sb_addr = smem_addr(s_b), sx_addr = smem_addr(s_x);
+  const uint32_t smid_addr = smem_addr(&s_mid[0][0]);
+  const int g = lane >> 2, cq = lane & 3;
   bool ok = true;
   uint32_t x_phase = 0, p_phase = 0;
   bool first = true;
-  int tiles_left = 0;
   for (int from = 0; from < p.bs; from += kFusedScan) {
     if (from > 0) {
       __syncthreads();
@@ -225,50 +247,80 @@ __global__ void __launch_bounds__(kFusedNT) apply_fused_kernel(const FusedArgs p
     for (int q0 = 0; q0 < ntok; q0 += TT) {
       const int nt = min(TT, ntok - q0);
       if (tid < nt) s_rows[tid] = fused_token_row(sl, q0 + tid);
+      if (klen % 16 != 0)
+        for (int e = tid; e < TT * 8; e += NT) s_x[(size_t)(e / 8) * kp + klen + (e % 8)] = Num<T>::from_f(0.f);
       __syncthreads();
-      if (tid == 0) {  // this tile's x rows (k-slice) and y rows (output block)
+      if (tid == 0 && m.y_tma && olen > 0) {  // this tile's y rows (output block); needed only by the expand
         fence_proxy_async_smem();
-        const uint32_t y_bytes = m.y_tma ? (uint32_t)nt * olen * sizeof(T) : 0u;
-        mbar_arrive_expect_tx(&bar_x, (uint32_t)nt * klen * sizeof(T) + y_bytes);
-        for (int t = 0; t < nt; ++t) {
-          if (klen > 0)
-            bulk_copy_g2s(s_x + (size_t)t * p.ks, xbase + (int64_t)s_rows[t] * p.x_stride + k0, klen * sizeof(T),
-                          &bar_x);
-          if (y_bytes > 0 && olen > 0)
-            bulk_copy_g2s(s_y + (size_t)t * p.ob_max, ybase + (int64_t)s_rows[t] * m.y_stride + o_lo,
-                          olen * sizeof(T), &bar_x);
+        mbar_arrive_expect_tx(&bar_x, (uint32_t)nt * olen * sizeof(T));
+        for (int t = 0; t < nt; ++t)
+          bulk_copy_g2s(s_y + (size_t)t * p.ob_max, ybase + (int64_t)s_rows[t] * m.y_stride + o_lo, olen * sizeof(T),
+                        &bar_x);
+      }
+      {  // this tile's x rows (k-slice): plain 16-byte loads by every thread (L2 hits)
+        const int kc = klen / 8;
+        for (int e = tid; e < nt * kc; e += NT) {
+          const int t = e / kc, c = e - t * kc;
+          const uint4 v = __ldcg(reinterpret_cast<const uint4*>(xbase + (int64_t)s_rows[t] * p.x_stride + k0) + c);
+          *reinterpret_cast<uint4*>(s_x + (size_t)t * kp + c * 8) = v;
         }
       }
       if (first) ok = mbar_wait(&bar_w, 0, p.status) && ok;
-      ok = mbar_wait(&bar_x, x_phase, p.status) && ok;
-      x_phase ^= 1u;
-      // split-K partials of this CTA's slice, one token at a time (decode tiles
-      // hold few tokens); the KG threads of a rank row reduce by shuffles
-      {
-        const int n = tid / KG, kg = tid % KG;
-        const uint4* arow = reinterpret_cast<const uint4*>(s_a + (size_t)n * p.ks);
-        for (int t = 0; t < nt; ++t) {
-          const uint4* xrow = reinterpret_cast<const uint4*>(s_x + (size_t)t * p.ks);
-          float acc = 0.f;
-          if (ok && n < rank) {
-            for (int c = kg; c < c_end; c += KG) {
-              float af[V], xf[V];
-              unpack16<T>(arow[c], af);
-              unpack16<T>(xrow[c], xf);
-#pragma unroll
-              for (int e = 0; e < V; ++e) acc = fmaf(xf[e], af[e], acc);
-            }
-          }
-#pragma unroll
-          for (int o = KG / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-          if (kg == 0) s_part[t][n] = acc;
+      __syncthreads();  // x tile complete
+      if (first && !b_dense) {  // B block: zero the stale columns past the rank once it has landed
+        cp_async_wait_all();
+        __syncthreads();
+        for (int e = tid; e < olen * (R - rank); e += NT) {
+          const int row = e / (R - rank), c = rank + e % (R - rank);
+          s_b[(size_t)row * R + c] = Num<T>::from_f(0.f);
         }
       }
-      if (first && !b_dense) cp_async_wait_all();
-      __syncthreads();  // s_part complete (and this CTA's B block, on the 16-byte-copy path)
+
+      // ---- shrink: split-K partials of this CTA's slice on tensor cores ----
+      {
+        float acc[RM / 8][4];
+#pragma unroll
+        for (int i = 0; i < RM / 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+        const int arow_l = lane & 15;
+        const int xrow = arow_l < nt ? arow_l : 0;  // rows past the tile repeat row 0
+        const uint32_t xa = sx_addr + (uint32_t)(xrow * kp + (lane >> 4) * 8) * 2u;
+        const int brow = lane & 7, bhalf = (lane >> 3) & 1;
+        if (ok) {
+          for (int kk = warp; kk < ksteps; kk += NW) {
+            uint32_t a0, a1, a2, a3;
+            ldsm_x4(xa + (uint32_t)kk * 32u, a0, a1, a2, a3);
+#pragma unroll
+            for (int i = 0; i < RM / 8; ++i) {
+              if (i * 8 < rank) {
+                uint32_t b0, b1;
+                ldsm_x2(sa_addr + (uint32_t)((i * 8 + brow) * kp + kk * 16 + bhalf * 8) * 2u, b0, b1);
+                mma_16816<T>(acc[i], a0, a1, a2, a3, b0, b1);
+              }
+            }
+          }
+        }
+        // rows g (< 8) of this warp's tiles -> warp partials
+        if (g < nt) {
+#pragma unroll
+          for (int i = 0; i < RM / 8; ++i) {
+            float* wr = s_wred + ((size_t)warp * TT + g) * RM + i * 8 + 2 * cq;
+            wr[0] = acc[i][0];
+            wr[1] = acc[i][1];
+          }
+        }
+      }
+      __syncthreads();
+      for (int e = tid; e < nt * RM; e += NT) {
+        const int t = e / RM, k = e - t * RM;
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) v += s_wred[((size_t)w * TT + t) * RM + k];
+        s_part[t][k] = v;
+      }
+      __syncthreads();  // s_part complete
       if (first) cluster_wait_acquire();  // every peer runs and has its barriers initialised
       first = false;
-      // push this CTA's partials into slot j of every peer's receive buffer
+      // ---- push this CTA's partials into slot j of every peer's receive buffer ----
       if (tid == 0) mbar_arrive_expect_tx(&bar_p, (uint32_t)cs * nt * RM * sizeof(float));
       {
         const uint32_t my_recv = smem_addr(s_recv + (size_t)j * TT * RM);
@@ -283,6 +335,7 @@ __global__ void __launch_bounds__(kFusedNT) apply_fused_kernel(const FusedArgs p
       }
       ok = mbar_wait(&bar_p, p_phase, p.status) && ok;
       p_phase ^= 1u;
+      // ---- gather: mid = sum of the cs partials in CTA order, rounded to T once ----
       for (int e = tid; e < TT * RM; e += NT) {
         const int t = e / RM, k = e - t * RM;
         float v = 0.f;
@@ -290,35 +343,59 @@ __global__ void __launch_bounds__(kFusedNT) apply_fused_kernel(const FusedArgs p
           for (int q = 0; q < cs; ++q) v += s_recv[((size_t)q * TT + t) * RM + k];
           if (j == 0 && m.mid != nullptr)
             static_cast<T*>(m.mid)[(int64_t)s_rows[t] * m.mid_stride + k] = Num<T>::from_f(v);
-          v = round_to<T>(v);
         }
-        s_mid[t][k] = v;
+        s_mid[t][k] = Num<T>::from_f(v);
       }
       __syncthreads();  // s_mid complete
-      // expand: this CTA's output block; consecutive threads own consecutive outputs
+      if (m.y_tma && olen > 0) {  // y rows staged during the shrink and exchange
+        ok = mbar_wait(&bar_x, x_phase, p.status) && ok;
+        x_phase ^= 1u;
+      }
+      // ---- expand: this CTA's output block on tensor cores, fused scaling + residual ----
       if (ok) {
-        for (int o = o_lo + tid; o < o_hi; o += NT) {
-          const uint4* brow = reinterpret_cast<const uint4*>(s_b + (size_t)(o - o_lo) * R);
-          for (int t = 0; t < nt; ++t) {
-            float acc = 0.f;
-            for (int c = 0; c < rc; ++c) {
-              float bf[V];
-              unpack16<T>(brow[c], bf);
-              const float4 m0 = *reinterpret_cast<const float4*>(&s_mid[t][c * V]);
-              const float4 m1 = *reinterpret_cast<const float4*>(&s_mid[t][c * V + 4]);
-              const float mv[V] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+        uint32_t am[RM / 16][4];
 #pragma unroll
-              for (int e = 0; e < V; ++e)  // stale weights past the rank may be NaN: masked
-                acc = fmaf(mv[e], (c * V + e < rank) ? bf[e] : 0.f, acc);
+        for (int kk = 0; kk < RM / 16; ++kk)
+          ldsm_x4(smid_addr + (uint32_t)((lane & 15) * MP + kk * 16 + (lane >> 4) * 8) * 2u, am[kk][0], am[kk][1],
+                  am[kk][2], am[kk][3]);
+        const int brow = lane & 7, bhalf = (lane >> 3) & 1;
+        const int ntiles = (olen + 7) / 8;
+        const int ksteps_r = (rank + 15) / 16;
+        for (int nb = warp; nb < ntiles; nb += NW) {
+          float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int kk = 0; kk < RM / 16; ++kk) {
+            if (kk < ksteps_r) {
+              uint32_t b0, b1 = 0u;
+              if (kk * 16 + 16 <= R) {
+                ldsm_x2(sb_addr + (uint32_t)((nb * 8 + brow) * R + kk * 16 + bhalf * 8) * 2u, b0, b1);
+              } else {  // R % 16 == 8: only the first 8 columns of this k-step exist in a B row
+                ldsm_x1(sb_addr + (uint32_t)((nb * 8 + brow) * R + kk * 16) * 2u, b0);
+              }
+              mma_16816<T>(acc, am[kk][0], am[kk][1], am[kk][2], am[kk][3], b0, b1);
             }
-            T* yp = ybase + (int64_t)s_rows[t] * m.y_stride + o;
-            const float yold = m.y_tma ? Num<T>::to_f(s_y[(size_t)t * p.ob_max + (o - o_lo)]) : ldcg_f<T>(yp);
-            *yp = Num<T>::from_f(round_to<T>(acc * scale) + yold);
+          }
+          if (g < nt) {  // row g of the tile: outputs o, o + 1
+            const int ol = nb * 8 + 2 * cq;
+            const int o = o_lo + ol;
+            T* yp = ybase + (int64_t)s_rows[g] * m.y_stride + o;
+            if (o + 1 < o_hi && m.y_tma) {
+              const T* ys = s_y + (size_t)g * p.ob_max + ol;
+              T v[2];
+              v[0] = Num<T>::from_f(round_to<T>(acc[0] * scale) + Num<T>::to_f(ys[0]));
+              v[1] = Num<T>::from_f(round_to<T>(acc[1] * scale) + Num<T>::to_f(ys[1]));
+              uint32_t u;
+              memcpy(&u, v, 4);
+              *reinterpret_cast<uint32_t*>(yp) = u;
+            } else {
+              if (o < o_hi) yp[0] = Num<T>::from_f(round_to<T>(acc[0] * scale) + ldcg_f<T>(yp));
+              if (o + 1 < o_hi) yp[1] = Num<T>::from_f(round_to<T>(acc[1] * scale) + ldcg_f<T>(yp + 1));
+            }
           }
         }
       }
-      tiles_left = (q0 + TT < ntok) || (from + kFusedScan < p.bs) ? 1 : 0;
-      if (tiles_left) cluster.sync();  // peers finished reading s_recv before the next pushes
+      const bool more = (q0 + TT < ntok) || (from + kFusedScan < p.bs);
+      if (more) cluster.sync();  // peers finished reading s_recv before the next pushes
       else __syncthreads();
     }
   }
@@ -331,7 +408,7 @@ __global__ void __launch_bounds__(kFusedNT) apply_fused_kernel(const FusedArgs p
     if (!b_dense) cp_async_wait_all();
   }
   if (!ok && tid == 0) {  // ok is only cleared inside a tile
-    mbar_wait(&bar_x, x_phase ^ 1u, p.status);
+    if (m.y_tma && olen > 0) mbar_wait(&bar_x, x_phase ^ 1u, p.status);
     mbar_wait(&bar_p, p_phase ^ 1u, p.status);
   }
 }
@@ -339,107 +416,165 @@ __global__ void __launch_bounds__(kFusedNT) apply_fused_kernel(const FusedArgs p
 namespace {
 
 template <typename T, int RM>
-cudaError_t go_fused(const FusedArgs& a, int cs, size_t smem, cudaStream_t st, bool pdl) {
-  auto kern = apply_fused_kernel<T, RM>;
-  // Function attributes are set once per instance (largest shared memory so far);
-  // whether a cluster shape can be placed at all is cached per (cs, smem KiB).
-  static std::mutex mu;
-  static int smem_set = 0;
-  static bool nonportable_set = false;
-  static std::map<std::pair<int, int>, bool> placeable;
-  {
+struct FusedLauncher {
+  std::mutex mu;
+  int smem_set = 0;
+  bool nonportable_set = false;
+  std::map<std::pair<int, int>, int> occ;  // (cs, smem KiB) -> resident CTAs per SM (0: cannot place)
+
+  // Resident CTAs per SM for this shape (0 when a cluster of cs cannot be placed).
+  int occupancy(int cs, size_t smem) {
     std::lock_guard<std::mutex> lock(mu);
-    cudaError_t e;
+    auto kern = apply_fused_kernel<T, RM>;
+    const int kib = (int)((smem + 1023) / 1024);
+    auto key = std::make_pair(cs, kib);
+    auto it = occ.find(key);
+    if (it != occ.end()) return it->second;
+    int result = 0;
     if (cs > 8 && !nonportable_set) {
-      e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-      if (e != cudaSuccess) return e;
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return occ[key] = 0;
+      }
       nonportable_set = true;
     }
-    const int kib = (int)((smem + 1023) / 1024);
     if (kib * 1024 > smem_set) {
-      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kib * 1024);
-      if (e != cudaSuccess) return e;
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kib * 1024) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return occ[key] = 0;
+      }
       smem_set = kib * 1024;
     }
-    auto key = std::make_pair(cs, kib);
-    auto it = placeable.find(key);
-    if (it == placeable.end()) {
-      cudaLaunchConfig_t q = {};
-      q.gridDim = dim3(cs, 1, 1);
-      q.blockDim = dim3(kFusedNT);
-      q.dynamicSmemBytes = (size_t)kib * 1024;
-      cudaLaunchAttribute qa[1];
-      qa[0].id = cudaLaunchAttributeClusterDimension;
-      qa[0].val.clusterDim.x = cs;
-      qa[0].val.clusterDim.y = 1;
-      qa[0].val.clusterDim.z = 1;
-      q.attrs = qa;
-      q.numAttrs = 1;
-      int clusters = 0;
-      e = cudaOccupancyMaxActiveClusters(&clusters, kern, &q);
-      if (e != cudaSuccess) {
-        (void)cudaGetLastError();
-        clusters = 0;
-      }
-      it = placeable.emplace(key, clusters > 0).first;
+    cudaLaunchConfig_t q = {};
+    q.gridDim = dim3(cs, 1, 1);
+    q.blockDim = dim3(kFusedNT);
+    q.dynamicSmemBytes = (size_t)kib * 1024;
+    cudaLaunchAttribute qa[1];
+    qa[0].id = cudaLaunchAttributeClusterDimension;
+    qa[0].val.clusterDim.x = cs;
+    qa[0].val.clusterDim.y = 1;
+    qa[0].val.clusterDim.z = 1;
+    q.attrs = qa;
+    q.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, kern, &q) != cudaSuccess) {
+      (void)cudaGetLastError();
+      clusters = 0;
     }
-    if (!it->second) return cudaErrorNotSupported;
+    int per_sm = 0;
+    if (clusters > 0 &&
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kFusedNT, (size_t)kib * 1024) != cudaSuccess) {
+      (void)cudaGetLastError();
+      per_sm = 0;
+    }
+    result = clusters > 0 ? (per_sm > 0 ? per_sm : 1) : 0;
+    return occ[key] = result;
   }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(cs, a.num_slots, a.n_mod);
-  cfg.blockDim = dim3(kFusedNT);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = cs;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
-  cfg.attrs = attr;
-  cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, kern, a);
+
+  cudaError_t launch(const FusedArgs& a, int cs, size_t smem, cudaStream_t st, bool pdl) {
+    auto kern = apply_fused_kernel<T, RM>;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(cs, a.num_slots, a.n_mod);
+    cfg.blockDim = dim3(kFusedNT);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, kern, a);
+  }
+};
+
+template <typename T, int RM>
+FusedLauncher<T, RM>& launcher() {
+  static FusedLauncher<T, RM> l;
+  return l;
+}
+
+size_t fused_smem(const FusedArgs& a, int rm, int ks, int ob_max, int cs) {
+  const int kp = padded_row(ks);
+  return (size_t)2 * ((size_t)a.R * kp + (size_t)ob_max * a.R + (size_t)kFusedTT * kp + (size_t)kFusedTT * ob_max) +
+         (size_t)4 * ((size_t)(kFusedNT / 32) * kFusedTT * rm + (size_t)cs * kFusedTT * rm);
+}
+
+int sm_count() {
+  static int n = [] {
+    int dev = 0, c = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return 148;
+    }
+    return c;
+  }();
+  return n;
+}
+
+template <typename T, int RM>
+cudaError_t launch_rm(FusedArgs a, cudaStream_t st, bool pdl) {
+  auto& l = launcher<T, RM>();
+  // Cluster size: fewest waves of CTAs for the whole launch (every slot counted,
+  // since which slots the batch uses is only known on the device), ties to the
+  // larger cluster (shorter per-CTA critical path).
+  int best_cs = 0, best_waves = 1 << 30;
+  size_t best_smem = 0;
+  FusedArgs best = a;
+  static const int forced_cs = [] {
+    const char* v = getenv("MLORA_FUSED_CLUSTER");  // tuning: force 2, 4, 8 or 16 CTAs per cluster
+    const int c = v != nullptr ? atoi(v) : 0;
+    return (c == 2 || c == 4 || c == 8 || c == 16) ? c : 0;
+  }();
+  for (int cs : {2, 4, 8, 16}) {
+    if (forced_cs != 0 && cs != forced_cs) continue;
+    FusedArgs c = a;
+    const int ks = ((a.in_dim + cs - 1) / cs + 15) / 16 * 16;
+    int ob_max = 8;
+    for (int i = 0; i < c.n_mod; ++i) {
+      FusedModule& m = c.mod[i];
+      m.ob = ((m.out_dim + cs - 1) / cs + 7) / 8 * 8;
+      ob_max = m.ob > ob_max ? m.ob : ob_max;
+      m.y_tma = (reinterpret_cast<uintptr_t>(m.y) % 16 == 0) && (m.y_stride % 8 == 0) && (m.out_dim % 8 == 0);
+    }
+    const size_t smem = fused_smem(c, RM, ks, ob_max, cs);
+    if (smem > 200 * 1024) continue;
+    const int per_sm = l.occupancy(cs, smem);
+    if (per_sm <= 0) continue;
+    const long long ctas = (long long)c.n_mod * c.num_slots * cs;
+    const int waves = (int)((ctas + (long long)sm_count() * per_sm - 1) / ((long long)sm_count() * per_sm));
+    if (waves < best_waves || (waves == best_waves && cs > best_cs)) {
+      c.ks = ks;
+      c.ob_max = ob_max;
+      best = c;
+      best_cs = cs;
+      best_waves = waves;
+      best_smem = smem;
+    }
+  }
+  if (best_cs == 0) return cudaErrorNotSupported;
+  return l.launch(best, best_cs, best_smem, st, pdl);
 }
 
 }  // namespace
 
-// Picks the cluster size so the per-CTA shared memory fits; returns
-// cudaErrorNotSupported when the shape is outside the fused kernel's range
-// (the caller then runs shrink and expand separately).
+// Returns cudaErrorNotSupported when the shape is outside the fused kernel's
+// range (the caller then runs shrink and expand separately).
 cudaError_t launch_apply_fused(FusedArgs a, int dtype, cudaStream_t st, bool pdl) {
   if (dtype != kBF16 && dtype != kF16) return cudaErrorNotSupported;
   if (a.n_mod < 1 || a.n_mod > kMaxFusedModules) return cudaErrorNotSupported;
   if (a.R > 64 || a.R % 8 != 0 || a.in_dim % 8 != 0) return cudaErrorNotSupported;
   const int rm = a.R <= 16 ? 16 : a.R <= 32 ? 32 : 64;
-  for (int cs : {8, 16}) {
-    int ks = (a.in_dim + cs - 1) / cs;
-    ks = (ks + 7) / 8 * 8;
-    int ob_max = 8;
-    for (int i = 0; i < a.n_mod; ++i) {
-      FusedModule& m = a.mod[i];
-      m.ob = ((m.out_dim + cs - 1) / cs + 7) / 8 * 8;
-      ob_max = m.ob > ob_max ? m.ob : ob_max;
-      m.y_tma = (reinterpret_cast<uintptr_t>(m.y) % 16 == 0) && (m.y_stride % 8 == 0) && (m.out_dim % 8 == 0);
-    }
-    const size_t smem = (size_t)2 * ((size_t)a.R * ks + (size_t)ob_max * a.R + (size_t)kFusedTT * ks +
-                                     (size_t)kFusedTT * ob_max) +
-                        (size_t)4 * cs * kFusedTT * rm;
-    if (smem > 200 * 1024) continue;
-    a.ks = ks;
-    a.ob_max = ob_max;
-    cudaError_t e;
-    if (dtype == kBF16)
-      e = rm == 16 ? go_fused<__nv_bfloat16, 16>(a, cs, smem, st, pdl)
-        : rm == 32 ? go_fused<__nv_bfloat16, 32>(a, cs, smem, st, pdl)
-                   : go_fused<__nv_bfloat16, 64>(a, cs, smem, st, pdl);
-    else
-      e = rm == 16 ? go_fused<__half, 16>(a, cs, smem, st, pdl)
-        : rm == 32 ? go_fused<__half, 32>(a, cs, smem, st, pdl)
-                   : go_fused<__half, 64>(a, cs, smem, st, pdl);
-    if (e != cudaErrorNotSupported) return e;
-  }
-  return cudaErrorNotSupported;
+  if (dtype == kBF16)
+    return rm == 16 ? launch_rm<__nv_bfloat16, 16>(a, st, pdl)
+         : rm == 32 ? launch_rm<__nv_bfloat16, 32>(a, st, pdl)
+                    : launch_rm<__nv_bfloat16, 64>(a, st, pdl);
+  return rm == 16 ? launch_rm<__half, 16>(a, st, pdl)
+       : rm == 32 ? launch_rm<__half, 32>(a, st, pdl)
+                  : launch_rm<__half, 64>(a, st, pdl);
 }
 
 }  // namespace mlora
