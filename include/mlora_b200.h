@@ -131,6 +131,29 @@ int mlora_apply_lora_group(const void* x, int64_t rows, int64_t in_dim, int64_t 
                            int32_t dtype, uint32_t* status, void* stream);
 
 /*
+ * Same result as mlora_apply_lora_group (two launches per projection: shrink,
+ * then expand), for callers that cannot allocate device memory: the
+ * intermediate mid lives in a 1 MiB device array owned by the library, so the
+ * caller passes only inputs and outputs and the call allocates nothing (no
+ * cudaMalloc, cudaFree or allocating library routine). Use it where a host
+ * gives this library no allocator, or where cudaMalloc's device
+ * synchronisation is not acceptable.
+ * Limit: rows * max_rank * element size <= 1 MiB (e.g. 32768 rows at bf16 and
+ * max_rank 16); larger calls return MLORA_ERR_INVALID_ARGUMENT.
+ * Every GPU that loads the library holds the 1 MiB until the process exits.
+ * The first call on a device looks up the array's device address (with that
+ * device current); make that first call before any stream capture. All calls
+ * on a device share the array: calls that overlap on the GPU race and give
+ * wrong results. Nothing in it needs to start at zero.
+ * This entry point has no counterpart in the reference project.
+ */
+int mlora_apply_lora_group_noalloc(const void* x, int64_t rows, int64_t in_dim, int64_t x_row_stride, int32_t n,
+                                   const void* const* a_stacks, const void* const* b_stacks, const int64_t* out_dims,
+                                   void* const* ys, const int64_t* y_row_strides, int64_t max_rank,
+                                   const mlora_kernel_input_metadata_t* meta, int32_t dtype, uint32_t* status,
+                                   void* stream);
+
+/*
  * RMSNorm: y[r, :] = dtype( x_f32 * rsqrt(mean(x_f32^2) + eps) * w_f32 ).
  * Row r of x starts at (r / inner) * stride_outer + (r % inner) * stride_inner
  * (elements); y is [rows, hidden] with row stride y_row_stride. w has

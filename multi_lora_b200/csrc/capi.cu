@@ -61,6 +61,10 @@ int check_meta(const mlora_kernel_input_metadata_t* m, int64_t rows) {
 
 }  // namespace
 
+namespace mlora {
+int report_error(int code, const char* msg) { return fail(code, "%s", msg); }
+}  // namespace mlora
+
 extern "C" {
 
 const char* mlora_last_error(void) { return g_err; }

@@ -92,6 +92,9 @@ struct FusedArgs {
 };
 
 cudaError_t launch_apply_fused(FusedArgs a, int dtype, cudaStream_t st, bool pdl);
+
+// Sets the message mlora_last_error() returns on this thread; returns `code`.
+int report_error(int code, const char* msg);
 cudaError_t launch_shrink(const ShrinkArgs& a, int dtype, bool out_f32, cudaStream_t st, bool pdl);
 cudaError_t launch_expand(const ExpandArgs& a, int dtype, bool mid_f32, cudaStream_t st, bool pdl);
 cudaError_t launch_rmsnorm(const RmsNormArgs& a, int dtype, cudaStream_t st, bool pdl);
