@@ -14,7 +14,16 @@ slots, so one step streams ~2.6 GB of adapter weights — far more than the
 126 MB L2, so no L2 flush is needed between steps. The step is captured
 once into a CUDA graph through the public API and replayed.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+With N > 1 GPUs (one process per GPU under torchrun) the same workload runs
+tensor-parallel over the N ranks (strong scaling: the job still processes
+64 tokens per step): q/k/v/gate/up are column-parallel (A replicated, B
+column-sharded, no collective); o/down are row-parallel (A row-sharded on the
+input dim, fp32 [T, r] shrink partials all-reduced over NCCL, B
+column-sharded into the rank's columns of the pre-all-reduce output).
+``--workload cfg5`` selects the Llama-3-70B-shaped TP decode config (80
+layers, hidden 8192, 128 adapters, 512 tokens) instead.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload cfg2|cfg5]
 
 Prints one JSON line (rank 0).
 """
@@ -40,16 +49,32 @@ sys.path.insert(0, str(ROOT))
 METRIC = "LoRA shrink+expand tokens/s and % HBM/TC roofline, 1/2/4/8 B200"
 UNIT = "tokens/s"
 
-# (name, in, out) of Llama-2-7B projections
-LLAMA2_7B = [("q", 4096, 4096), ("k", 4096, 4096), ("v", 4096, 4096), ("o", 4096, 4096),
-             ("gate", 4096, 11008), ("up", 4096, 11008), ("down", 11008, 4096)]
-HIDDEN = 4096
-LAYERS = 32
-TOKENS = 64
-ADAPTERS = 32
-RANK = 16
-SCALING = 32 / 16
 EPS = 1e-6
+COLUMN, ROW = "column", "row"
+GROUPS = (("q", "k", "v"), ("o",), ("gate", "up"), ("down",))  # calls per layer, in dependency order
+
+
+class Workload:
+    """A Llama-shaped decode workload: per layer q/k/v/o/gate/up/down LoRA
+    projections and two RMSNorms; ``tokens`` tokens with uniform adapter ids."""
+
+    def __init__(self, name, desc, hidden, kv, inter, layers, tokens, adapters, rank, alpha):
+        self.name, self.desc = name, desc
+        self.hidden, self.layers, self.tokens = hidden, layers, tokens
+        self.adapters, self.rank, self.scaling = adapters, rank, alpha / rank
+        # (name, in, out, tensor-parallel kind)
+        self.projs = [("q", hidden, hidden, COLUMN), ("k", hidden, kv, COLUMN), ("v", hidden, kv, COLUMN),
+                      ("o", hidden, hidden, ROW), ("gate", hidden, inter, COLUMN), ("up", hidden, inter, COLUMN),
+                      ("down", inter, hidden, ROW)]
+        self.inter = inter
+
+
+WORKLOADS = {
+    "cfg2": Workload("cfg2", "Llama-2-7B-shaped decode: 32 layers x 7 LoRA projections + 2 RMSNorm, 64 tokens, "
+                             "32 adapters r16 (alpha 32), bf16", 4096, 4096, 11008, 32, 64, 32, 16, 32),
+    "cfg5": Workload("cfg5", "Llama-3-70B-shaped decode: 80 layers x 7 LoRA projections + 2 RMSNorm, 512 tokens, "
+                             "128 adapters r16 (alpha 32), bf16", 8192, 1024, 28672, 80, 512, 128, 16, 32),
+}
 
 
 def peaks() -> dict:
@@ -60,103 +85,122 @@ def peaks() -> dict:
     return {"hbm_gbs": 6650.0, "src": "fallback"}
 
 
-def cfg2_routing(seed: int = 0):
-    """Adapter id per token (uniform over 32) -> grouped segments (adjacent equal ids merge)."""
+def routing(wl: Workload, seed: int = 0):
+    """Adapter id per token (uniform) -> grouped segments (adjacent equal ids merge); adapter i in slot i."""
     from multi_lora_b200.batch_info import BatchLoRAInfo, group_rows
 
     g = torch.Generator().manual_seed(seed)
-    ids = torch.randint(0, ADAPTERS, (TOKENS,), generator=g).tolist()
-    names, lens = group_rows(ids, [])  # adapter i lives in slot i
-    info = BatchLoRAInfo(weight_indices=list(names), lora_ranks=[RANK] * ADAPTERS,
-                         scalings=[SCALING] * ADAPTERS)
+    ids = torch.randint(0, wl.adapters, (wl.tokens,), generator=g).tolist()
+    names, lens = group_rows(ids, [])
+    info = BatchLoRAInfo(weight_indices=list(names), lora_ranks=[wl.rank] * wl.adapters,
+                         scalings=[wl.scaling] * wl.adapters)
     return ids, info, lens
 
 
-def algorithmic_bytes(ids) -> dict:
-    """Bytes a perfect kernel moves per step (adapter rows up to the rank only)."""
+def shard_dims(wl: Workload, tp: int) -> dict:
+    """Per projection on one TP rank: (input dim read, B rows held, y columns)."""
+    dims = {}
+    for name, n_in, n_out, kind in wl.projs:
+        if tp == 1:
+            dims[name] = (n_in, n_out, n_out)
+        elif kind == COLUMN:
+            dims[name] = (n_in, n_out // tp, n_out // tp)
+        else:  # row-parallel: x and A sharded on in; B column-sharded into the full-width partial output
+            dims[name] = (n_in // tp, n_out // tp, n_out)
+    return dims
+
+
+def algorithmic_bytes(wl: Workload, ids, tp: int) -> dict:
+    """Bytes a perfect kernel moves per step on one rank: A rows up to the rank
+    of each distinct adapter, B columns up to the rank, x once, y read and
+    written once, mid written and read once (per projection)."""
     d = len(set(ids))
-    T, es = TOKENS, 2
-    shrink = expand = 0
-    for _, n_in, n_out in LLAMA2_7B:
-        shrink += d * RANK * n_in * es + T * n_in * es + T * RANK * es
-        expand += d * RANK * n_out * es + 2 * T * n_out * es + T * RANK * es
-    rms = 2 * (2 * T * HIDDEN * es + HIDDEN * es)
-    return {"shrink": shrink * LAYERS, "expand": expand * LAYERS, "rmsnorm": rms * LAYERS,
-            "distinct_adapters": d}
+    T, es, r = wl.tokens, 2, wl.rank
+    dims = shard_dims(wl, tp)
+    lora = 0
+    for name, *_ in wl.projs:
+        i, o, _ = dims[name]
+        lora += d * r * i * es + d * r * o * es + T * i * es + 2 * T * o * es + 2 * T * r * es
+    rms = 2 * (2 * T * wl.hidden * es + wl.hidden * es)
+    return {"lora": lora * wl.layers, "rmsnorm": rms * wl.layers, "distinct_adapters": d}
 
 
 class Layer:
     pass
 
 
-def build_workload(dev, seed: int = 0):
-    """Per-layer adapter slots and activations, generated on the device."""
-    g = torch.Generator(device=dev).manual_seed(1234 + seed)
+def build_workload(wl: Workload, dev, tp_rank: int = 0, tp: int = 1):
+    """Per-layer adapter slot stacks (this rank's shards) and activations, generated on the device."""
+    g = torch.Generator(device=dev).manual_seed(1234 + 7919 * tp_rank)
     dt = torch.bfloat16
+    T, K, R = wl.tokens, wl.adapters, wl.rank
+    dims = shard_dims(wl, tp)
     layers = []
-    for _ in range(LAYERS):
+    for _ in range(wl.layers):
         L = Layer()
-        L.A, L.B, L.x, L.y = {}, {}, {}, {}
-        for name, n_in, n_out in LLAMA2_7B:
+        L.A, L.B, L.y = {}, {}, {}
+        for name, n_in, _, _ in wl.projs:
+            i, o, ycols = dims[name]
             bound = 1.0 / math.sqrt(n_in)  # kaiming-uniform(a=sqrt(5)) of an [r, in] weight
-            L.A[name] = ((torch.rand(ADAPTERS, RANK, n_in, generator=g, device=dev) * 2 - 1) * bound).to(dt)
-            L.B[name] = (torch.randn(ADAPTERS, n_out, RANK, generator=g, device=dev) * 0.02).to(dt)
-            L.y[name] = torch.randn(TOKENS, n_out, generator=g, device=dev).to(dt)
-        L.h1 = torch.randn(TOKENS, HIDDEN, generator=g, device=dev).to(dt)
-        L.h2 = torch.randn(TOKENS, HIDDEN, generator=g, device=dev).to(dt)
-        L.w1 = (1 + 0.1 * torch.randn(HIDDEN, generator=g, device=dev)).to(dt)
-        L.w2 = (1 + 0.1 * torch.randn(HIDDEN, generator=g, device=dev)).to(dt)
-        L.xn1 = torch.empty(TOKENS, HIDDEN, device=dev, dtype=dt)
-        L.xn2 = torch.empty(TOKENS, HIDDEN, device=dev, dtype=dt)
-        L.xo = torch.randn(TOKENS, HIDDEN, generator=g, device=dev).to(dt)       # attention output
-        L.xd = torch.randn(TOKENS, 11008, generator=g, device=dev).to(dt)        # act(gate) * up
-        L.x = {"q": L.xn1, "k": L.xn1, "v": L.xn1, "o": L.xo, "gate": L.xn2, "up": L.xn2, "down": L.xd}
+            L.A[name] = ((torch.rand(K, R, i, generator=g, device=dev) * 2 - 1) * bound).to(dt)
+            L.B[name] = (torch.randn(K, o, R, generator=g, device=dev) * 0.02).to(dt)
+            L.y[name] = torch.randn(T, ycols, generator=g, device=dev).to(dt)
+        H = wl.hidden
+        L.h1 = torch.randn(T, H, generator=g, device=dev).to(dt)
+        L.h2 = torch.randn(T, H, generator=g, device=dev).to(dt)
+        L.w1 = (1 + 0.1 * torch.randn(H, generator=g, device=dev)).to(dt)
+        L.w2 = (1 + 0.1 * torch.randn(H, generator=g, device=dev)).to(dt)
+        L.xn1 = torch.empty(T, H, device=dev, dtype=dt)
+        L.xn2 = torch.empty(T, H, device=dev, dtype=dt)
+        xo = torch.randn(T, dims["o"][0], generator=g, device=dev).to(dt)      # attention output (this rank's part)
+        xd = torch.randn(T, dims["down"][0], generator=g, device=dev).to(dt)   # act(gate) * up (this rank's part)
+        L.x = {"q": L.xn1, "k": L.xn1, "v": L.xn1, "o": xo, "gate": L.xn2, "up": L.xn2, "down": xd}
         layers.append(L)
     return layers
 
 
-def run_step(layers, be, parts=("rmsnorm", "lora"), grouped=True):
-    """One forward of the LoRA hot path over all layers.
+def run_step(wl: Workload, layers, be, parts=("rmsnorm", "lora"), grouped=True, tp=1, tp_rank=0):
+    """One forward of the LoRA hot path over all layers, in the model's
+    dependency order: rmsnorm -> {q,k,v} -> o -> rmsnorm -> {gate,up} -> down.
 
-    grouped: q/k/v (shared input) and gate/up (shared input) each go through one
-    ``apply_lora_group`` call, which is the dependency structure of the model
-    (rmsnorm -> {q,k,v} -> o -> rmsnorm -> {gate,up} -> down); otherwise every
-    projection is its own ``apply_lora`` call.
+    grouped: q/k/v and gate/up (shared input) each go through one
+    ``apply_lora_group`` call; otherwise one ``apply_lora`` per projection.
+    tp > 1: o and down are row-parallel (``row_parallel_apply``: shrink
+    partials, NCCL all-reduce, expand), the rest column-parallel.
     """
     from multi_lora_b200.rmsnorm import rmsnorm_out
+    from multi_lora_b200.tensor_parallel import row_parallel_apply
 
-    if grouped and "lora" in parts:
-        for L in layers:
-            if "rmsnorm" in parts:
-                rmsnorm_out(L.h1, L.w1, EPS, L.xn1)
-            qkv = ("q", "k", "v")
-            be.apply_lora_group(L.xn1, [L.A[n] for n in qkv], [L.B[n] for n in qkv], [L.y[n] for n in qkv])
-            be.apply_lora(L.x["o"], L.A["o"], L.B["o"], L.y["o"])
-            if "rmsnorm" in parts:
-                rmsnorm_out(L.h2, L.w2, EPS, L.xn2)
-            gu = ("gate", "up")
-            be.apply_lora_group(L.xn2, [L.A[n] for n in gu], [L.B[n] for n in gu], [L.y[n] for n in gu])
-            be.apply_lora(L.x["down"], L.A["down"], L.B["down"], L.y["down"])
-        return
+    kinds = {name: kind for name, _, _, kind in wl.projs}
     for L in layers:
-        if "rmsnorm" in parts:
-            rmsnorm_out(L.h1, L.w1, EPS, L.xn1)
-        for name in ("q", "k", "v", "o"):
-            if "lora" in parts:
-                be.apply_lora(L.x[name], L.A[name], L.B[name], L.y[name])
-            elif "shrink" in parts:
-                be.run_lora_a_sgemm(L.x[name], L.A[name])
-            elif "expand" in parts:
-                be.run_lora_b_sgemm(be._mid[:TOKENS], L.B[name], base_output=L.y[name])
-        if "rmsnorm" in parts:
-            rmsnorm_out(L.h2, L.w2, EPS, L.xn2)
-        for name in ("gate", "up", "down"):
-            if "lora" in parts:
-                be.apply_lora(L.x[name], L.A[name], L.B[name], L.y[name])
-            elif "shrink" in parts:
-                be.run_lora_a_sgemm(L.x[name], L.A[name])
-            elif "expand" in parts:
-                be.run_lora_b_sgemm(be._mid[:TOKENS], L.B[name], base_output=L.y[name])
+        for grp in GROUPS:
+            if "rmsnorm" in parts and grp[0] in ("q", "gate"):
+                rmsnorm_out(L.h1 if grp[0] == "q" else L.h2, L.w1 if grp[0] == "q" else L.w2, EPS,
+                            L.xn1 if grp[0] == "q" else L.xn2)
+            if "lora" not in parts:
+                continue
+            if tp > 1 and kinds[grp[0]] == ROW:
+                for n in grp:
+                    row_parallel_apply(be, L.x[n], L.A[n], L.B[n], L.y[n], tp_rank, tp)
+            elif grouped and len(grp) > 1:
+                be.apply_lora_group(L.x[grp[0]], [L.A[n] for n in grp], [L.B[n] for n in grp],
+                                    [L.y[n] for n in grp])
+            else:
+                for n in grp:
+                    be.apply_lora(L.x[n], L.A[n], L.B[n], L.y[n])
+
+
+def launches_per_layer(wl: Workload, grouped: bool, fused: bool, tp: int) -> dict:
+    """Our kernel launches per layer (torch's memsets and NCCL's kernels not counted)."""
+    kinds = {name: kind for name, _, _, kind in wl.projs}
+    lora = 0
+    for grp in GROUPS:
+        if tp > 1 and kinds[grp[0]] == ROW:
+            lora += 2 * len(grp)  # shrink (fp32 partials) + expand
+        else:
+            calls = 1 if grouped else len(grp)
+            lora += calls * (1 if fused else 2)
+    return {"lora": lora, "rmsnorm": 2}
 
 
 def capture(fn):
@@ -240,17 +284,18 @@ def read_traffic() -> dict:
 class CpuReference:
     """The reference's per-segment Torch path (oracle port) on the host cores.
 
-    One sample = one whole cfg2 layer (2 RMSNorms + 7 projections,
-    shrink+expand, bf16); throughput is scaled to the 32-layer step
-    (tokens per step / (32 x seconds per layer)).
+    One sample = one whole layer of the workload (2 RMSNorms + 7 projections,
+    shrink+expand, bf16, unsharded); throughput is scaled to the full step
+    (tokens per step / (layers x seconds per layer)).
     """
 
-    def __init__(self):
+    def __init__(self, wl: Workload):
         from oracle.torch_port import TorchPortBackend, rmsnorm
 
+        self.wl = wl
         self.threads = os.cpu_count() or 1
         torch.set_num_threads(self.threads)
-        ids, info, lens = cfg2_routing(0)
+        ids, info, lens = routing(wl, 0)
         indptr = [0]
         for n in lens:
             indptr.append(indptr[-1] + n)
@@ -261,13 +306,13 @@ class CpuReference:
         self.rmsnorm = rmsnorm
         g = torch.Generator().manual_seed(7)
         dt = torch.bfloat16
-        self.A = {n: ((torch.rand(ADAPTERS, RANK, i, generator=g) * 2 - 1) / math.sqrt(i)).to(dt)
-                  for n, i, _ in LLAMA2_7B}
-        self.B = {n: (torch.randn(ADAPTERS, o, RANK, generator=g) * 0.02).to(dt) for n, _, o in LLAMA2_7B}
-        self.y = {n: torch.randn(TOKENS, o, generator=g).to(dt) for n, _, o in LLAMA2_7B}
-        self.h = torch.randn(TOKENS, HIDDEN, generator=g).to(dt)
-        self.w = torch.ones(HIDDEN, dtype=dt)
-        self.xd = torch.randn(TOKENS, 11008, generator=g).to(dt)
+        K, R, T = wl.adapters, wl.rank, wl.tokens
+        self.A = {n: ((torch.rand(K, R, i, generator=g) * 2 - 1) / math.sqrt(i)).to(dt) for n, i, _, _ in wl.projs}
+        self.B = {n: (torch.randn(K, o, R, generator=g) * 0.02).to(dt) for n, _, o, _ in wl.projs}
+        self.y = {n: torch.randn(T, o, generator=g).to(dt) for n, _, o, _ in wl.projs}
+        self.h = torch.randn(T, wl.hidden, generator=g).to(dt)
+        self.w = torch.ones(wl.hidden, dtype=dt)
+        self.xd = torch.randn(T, wl.inter, generator=g).to(dt)
 
     def layer(self) -> float:
         t0 = time.perf_counter()
@@ -288,17 +333,19 @@ class CpuReference:
             el += self.layer()
             n += 1
         per_layer = el / n
-        return {"value": TOKENS / (LAYERS * per_layer), "unit": UNIT, "cores": self.threads, "kind": "port",
-                "sample": f"{n} cfg2 layers (2 RMSNorm + 7 projections, bf16) in {el:.1f}s; x32 layers per step",
+        wl = self.wl
+        return {"value": wl.tokens / (wl.layers * per_layer), "unit": UNIT, "cores": self.threads, "kind": "port",
+                "sample": f"{n} {wl.name} layers (2 RMSNorm + 7 projections, bf16) in {el:.1f}s; "
+                          f"x{wl.layers} layers per step",
                 "per_layer_ms": round(per_layer * 1e3, 3)}
 
 
-def config_block(n: int) -> dict:
-    return {"workload": "cfg2 Llama-2-7B-shaped decode: 32 layers x 7 LoRA projections + 2 RMSNorm, "
-                        "64 tokens, 32 adapters r16 (alpha 32), bf16",
-            "global_batch": TOKENS * n, "seq_len": 1, "layers": LAYERS, "adapters": ADAPTERS, "rank": RANK,
-            "parallelism": f"replicas{n}" if n > 1 else "single",
-            "l2": "no flush: each step streams ~2.6 GB of distinct per-layer adapter weights (> 126 MB L2)"}
+def config_block(wl: Workload, n: int) -> dict:
+    return {"workload": wl.desc, "global_batch": wl.tokens, "seq_len": 1, "layers": wl.layers,
+            "adapters": wl.adapters, "rank": wl.rank,
+            "parallelism": f"tp{n} (q/k/v/gate/up column-parallel, o/down row-parallel + NCCL all-reduce of "
+                           f"fp32 [T, r] partials)" if n > 1 else "single",
+            "l2": "no flush: each step streams the distinct per-layer adapter weights (GBs, > 126 MB L2)"}
 
 
 def main() -> None:
@@ -307,10 +354,12 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ungrouped", action="store_true",
                     help="one apply_lora call per projection instead of grouping q/k/v and gate/up")
     args = ap.parse_args()
+    wl = WORKLOADS[args.workload]
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -321,28 +370,31 @@ def main() -> None:
         # the reference's CPU path on the host cores; rank 0 alone
         if rank != 0:
             return
-        ref = CpuReference()
+        ref = CpuReference(wl)
         for _ in range(args.warmup):
             ref.layer()
         per_layer = statistics.mean(ref.layer() for _ in range(args.steps))
-        value = TOKENS / (LAYERS * per_layer)
+        value = wl.tokens / (wl.layers * per_layer)
         out = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": n,
-               "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_layer * LAYERS * 1e3,
-               "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-               "data": "synthetic", "config": config_block(1),
+               "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_layer * wl.layers * 1e3,
+               "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+               "data": "synthetic", "config": config_block(wl, n),
                "cpu_baseline": {"value": value, "unit": UNIT, "cores": ref.threads, "kind": "port",
-                                "sample": f"each step: one cfg2 layer (2 RMSNorm + 7 projections), x32 layers"},
+                                "sample": f"each step: one {wl.name} layer (2 RMSNorm + 7 projections, unsharded), "
+                                          f"x{wl.layers} layers"},
                "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(out), flush=True)
         return
 
+    tp = world
     if world > 1:
         import datetime
 
         import torch.distributed as dist
 
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local if world > 1 else 0)
     torch.cuda.set_device(dev)
 
@@ -351,19 +403,25 @@ def main() -> None:
     from multi_lora_b200.batch_info import empty_kernel_input_metadata, write_kernel_input_metadata
 
     _native.ops()
-    ids, info, lens = cfg2_routing(0)
-    layers = build_workload(dev, seed=rank)
+    ids, info, lens = routing(wl, 0)  # the same tokens on every TP rank
+    layers = build_workload(wl, dev, tp_rank=rank, tp=tp)
     be = CudaLoRABackend()
     meta = write_kernel_input_metadata(empty_kernel_input_metadata(device=dev, dtype=torch.bfloat16), info,
                                        device=dev, dtype=torch.bfloat16, seq_lens=lens)
     be.set_kernel_input_metadata(meta)
+    if world > 1:  # communicator up before any capture
+        w = torch.ones(1, device=dev)
+        torch.distributed.all_reduce(w)
     torch.cuda.synchronize()
 
     grouped = not args.ungrouped
-    step_graph = capture(lambda: run_step(layers, be, grouped=grouped))
+    graphs = []
+    step_graph = capture(lambda: run_step(wl, layers, be, grouped=grouped, tp=tp, tp_rank=rank))
+    graphs.append(step_graph)
+    be.apply_lora(layers[0].x["q"], layers[0].A["q"], layers[0].B["q"], layers[0].y["q"].clone())
     fused = _native.capi().mlora_last_apply_path() == 1
-    lora_calls = 4 if grouped else 7
-    launches_per_step = LAYERS * (2 + lora_calls * (1 if fused else 2))
+    per_layer = launches_per_layer(wl, grouped, fused, tp)
+    launches_per_step = wl.layers * (per_layer["lora"] + per_layer["rmsnorm"])
 
     for _ in range(args.warmup):
         step_graph.replay()
@@ -372,6 +430,13 @@ def main() -> None:
     def barrier():
         if world > 1:
             torch.distributed.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
 
     visible = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
     dev_index = dev.index if dev.index is not None else 0
@@ -388,30 +453,28 @@ def main() -> None:
     torch.cuda.synchronize()
     barrier()
     clk = clocks.stop()
-    ms = e0.elapsed_time(e1) / args.steps
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
-    value = TOKENS * n / (ms / 1e3)
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    value = wl.tokens / (ms / 1e3)
 
     # ---- roofline of the dominant kernel (the apply_lora launches), timed alone ----
-    ab = algorithmic_bytes(ids)
+    ab = algorithmic_bytes(wl, ids, tp)
     pk = peaks()
-    g_lora = capture(lambda: run_step(layers, be, parts=("lora",), grouped=grouped))
-    lora_ms = time_graph(g_lora, max(20, args.steps // 4))
-    del g_lora
-    g_rms = capture(lambda: run_step(layers, be, parts=("rmsnorm",)))
-    rms_ms = time_graph(g_rms, max(20, args.steps // 4))
-    del g_rms
-    lora_launches = LAYERS * lora_calls * (1 if fused else 2)
-    lora_bytes = ab["shrink"] + ab["expand"]
-    per_launch_bytes = lora_bytes / lora_launches
+    g_lora = capture(lambda: run_step(wl, layers, be, parts=("lora",), grouped=grouped, tp=tp, tp_rank=rank))
+    graphs.append(g_lora)
+    lora_ms = max_over_ranks(time_graph(g_lora, max(20, args.steps // 4)))
+    g_rms = capture(lambda: run_step(wl, layers, be, parts=("rmsnorm",), tp=tp, tp_rank=rank))
+    graphs.append(g_rms)
+    rms_ms = max_over_ranks(time_graph(g_rms, max(20, args.steps // 4)))
+    lora_launches = wl.layers * per_layer["lora"]
+    per_launch_bytes = ab["lora"] / lora_launches
     per_launch_ms = lora_ms / lora_launches
     achieved = per_launch_bytes / (per_launch_ms / 1e3) / 1e9
-    kernel = "apply_fused_kernel" if fused else "shrink_kernel+expand_kernel"
-    traffic = read_traffic().get(kernel)
-    step_bytes = lora_bytes + ab["rmsnorm"]
+    if tp > 1:
+        kernel = "lora part per rank: apply_fused_kernel (column) + shrink/expand + NCCL all-reduce (row)"
+    else:
+        kernel = "apply_fused_kernel" if fused else "shrink_kernel+expand_kernel"
+    traffic = read_traffic().get(kernel) if wl.name == "cfg2" and tp == 1 else None
+    step_bytes = ab["lora"] + ab["rmsnorm"]
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                 "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": traffic, "kernel": kernel,
                 "peak_source": pk["src"], "bytes_per_launch": round(per_launch_bytes),
@@ -420,16 +483,18 @@ def main() -> None:
     step_roofline = {"bytes_per_step": step_bytes, "achieved": round(step_achieved, 1),
                      "frac": round(step_achieved / pk["hbm_gbs"], 4), "unit": "GB/s",
                      "lora_ms_alone": round(lora_ms, 4), "rmsnorm_ms_alone": round(rms_ms, 4),
-                     "distinct_adapters": ab["distinct_adapters"]}
+                     "distinct_adapters": ab["distinct_adapters"], "per_rank": tp > 1}
     if grouped:  # the same work as one apply_lora call per projection, for comparison
-        g_u = capture(lambda: run_step(layers, be, grouped=False))
-        step_roofline["ungrouped_ms_per_step"] = round(time_graph(g_u, max(20, args.steps // 4)), 4)
-        del g_u
+        g_u = capture(lambda: run_step(wl, layers, be, grouped=False, tp=tp, tp_rank=rank))
+        graphs.append(g_u)
+        step_roofline["ungrouped_ms_per_step"] = round(max_over_ranks(time_graph(g_u, max(20, args.steps // 4))), 4)
 
     # ---- e2e: public API with host buffers, copies inside the timed region ----
-    h_in = torch.randn(TOKENS, HIDDEN).bfloat16().pin_memory()
-    y_out = torch.empty(TOKENS, HIDDEN, dtype=torch.bfloat16).pin_memory()
+    last = layers[-1].y["down"]
+    h_in = torch.randn(wl.tokens, wl.hidden).bfloat16().pin_memory()
+    y_out = torch.empty(tuple(last.shape), dtype=torch.bfloat16).pin_memory()
     meta_bytes = meta._packed.words * 4 if meta._packed is not None else 0
+    barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     e2 = torch.cuda.Event(enable_timing=True)
@@ -439,16 +504,12 @@ def main() -> None:
         write_kernel_input_metadata(meta, info, device=dev, dtype=torch.bfloat16, seq_lens=lens)
         layers[0].h1.copy_(h_in, non_blocking=True)
         step_graph.replay()
-        y_out.copy_(layers[-1].y["down"], non_blocking=True)
+        y_out.copy_(last, non_blocking=True)
         st.synchronize()
     e3.record(st)
     e3.synchronize()
-    e2e_ms = max(e2.elapsed_time(e3), (time.perf_counter() - t0) * 1e3) / args.steps
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e = {"value": TOKENS * n / (e2e_ms / 1e3), "unit": UNIT,
+    e2e_ms = max_over_ranks(max(e2.elapsed_time(e3), (time.perf_counter() - t0) * 1e3) / args.steps)
+    e2e = {"value": wl.tokens / (e2e_ms / 1e3), "unit": UNIT,
            "h2d_bytes_per_step": meta_bytes + h_in.numel() * 2, "d2h_bytes_per_step": y_out.numel() * 2,
            "ms_per_step": e2e_ms,
            "path": "write_kernel_input_metadata (pinned H2D) + input hidden H2D + graph of the public-API "
@@ -456,19 +517,25 @@ def main() -> None:
 
     cpu = None
     if rank == 0 and n == 1 and not args.no_cpu_baseline:
-        cpu = CpuReference().measure()
+        cpu = CpuReference(wl).measure()
 
     if rank == 0:
         out = {"metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": n, "steps": args.steps,
                "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
-               "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+               "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
                "data": "synthetic (seeded; random-init adapters of the named shapes)",
-               "config": config_block(n), "roofline": roofline, "step_roofline": step_roofline,
+               "config": config_block(wl, n), "roofline": roofline, "step_roofline": step_roofline,
                "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
                "clocks": clk, "pdl": _native.get_pdl(), "grouped": grouped, "fused_path": fused}
         print(json.dumps(out), flush=True)
-    del step_graph
+    # graphs that hold NCCL calls go before the process group
+    del step_graph, g_lora, g_rms
+    if grouped:
+        del g_u
+    graphs.clear()
+    torch.cuda.synchronize()
     if world > 1:
+        torch.distributed.barrier()
         torch.distributed.destroy_process_group()
 
 

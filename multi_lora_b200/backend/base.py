@@ -19,6 +19,7 @@ class LoRABackend(ABC):
         self.kernel_input_metadata: Optional[KernelInputMetaData] = None
         # resident (rows, max_rank) shrink output, reused while it fits (base.py:24-38)
         self._mid = torch.empty((0, 0))
+        self._partial = torch.empty((0, 0))
 
     def mid_buffer(self, rows: int, max_rank: int, like: torch.Tensor) -> torch.Tensor:
         """A (rows, max_rank) buffer; the same storage is reused while it fits.
@@ -29,6 +30,24 @@ class LoRABackend(ABC):
         if m.shape[0] < rows or m.shape[1] != max_rank or m.device != like.device or m.dtype != like.dtype:
             self._mid = torch.empty((rows, max_rank), dtype=like.dtype, device=like.device)
         return self._mid[:rows]
+
+    def partial_buffer(self, rows: int, max_rank: int, like: torch.Tensor) -> torch.Tensor:
+        """A resident fp32 (rows, max_rank) buffer for tensor-parallel shrink
+        partials (same reuse rule as ``mid_buffer``)."""
+        m = self._partial
+        if m.shape[0] < rows or m.shape[1] != max_rank or m.device != like.device:
+            self._partial = torch.empty((rows, max_rank), dtype=torch.float32, device=like.device)
+        return self._partial[:rows]
+
+    def shrink_partial(self, x: torch.Tensor, a_shard: torch.Tensor) -> torch.Tensor:
+        """Tensor-parallel shrink: the unrounded fp32 ``x @ A[slot, :rank].T``
+        of this rank's input slice, zero where no adapter column is written."""
+        raise NotImplementedError(f"{type(self).__name__} has no tensor-parallel shrink")
+
+    def expand_partial(self, partial: torch.Tensor, b_shard: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+        """Tensor-parallel expand from the all-reduced fp32 ``partial`` (rounded
+        to y's dtype first, as the unsharded mid is) into ``y`` in place."""
+        raise NotImplementedError(f"{type(self).__name__} has no tensor-parallel expand")
 
     def set_kernel_input_metadata(self, metadata: KernelInputMetaData) -> None:
         """Bind this step's segment/slot routing."""

@@ -122,6 +122,25 @@ class CudaLoRABackend(LoRABackend):
                 o.copy_(t)
         return outs
 
+    def shrink_partial(self, x: torch.Tensor, a_shard: torch.Tensor) -> torch.Tensor:
+        """fp32 shrink partials of this rank's input slice into the resident
+        partial buffer (zeroed first, so the all-reduce sums only real terms)."""
+        meta = self._meta()
+        x = self._check_x(x, "x")
+        part = self.partial_buffer(x.shape[0], a_shard.shape[-2], x)
+        part.zero_()
+        return self._ops.sgemm_lora_a(
+            x, a_shard.contiguous(), _i32(meta.seg_lens), _i32(meta.seg_indptr), _i32(meta.weight_indices),
+            _i32(meta.lora_ranks), int(meta.bs), int(meta.max_len), part, self.stack_num,
+            self.status_word(x.device))
+
+    def expand_partial(self, partial: torch.Tensor, b_shard: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+        """Expand from the all-reduced fp32 partials (the kernel rounds them to
+        y's dtype before the product) into ``y`` (a column slice) in place."""
+        if partial.dtype != torch.float32:
+            raise TypeError("mlora: expand_partial expects the fp32 partial buffer")
+        return self.run_lora_b_sgemm(partial, b_shard, base_output=y)
+
     def run_lora_b_sgemm(
         self,
         x: torch.Tensor,
