@@ -190,16 +190,25 @@ def run_step(wl: Workload, layers, be, parts=("rmsnorm", "lora"), grouped=True, 
                     be.apply_lora(L.x[n], L.A[n], L.B[n], L.y[n])
 
 
-def launches_per_layer(wl: Workload, grouped: bool, fused: bool, tp: int) -> dict:
-    """Our kernel launches per layer (torch's memsets and NCCL's kernels not counted)."""
+APPLY_PATH_NAMES = {1: "fused", 2: "split", 3: "stream"}
+APPLY_KERNELS = {1: "apply_fused_kernel", 2: "shrink_kernel+expand_kernel",
+                 3: "lora_shrink_stream_kernel+lora_expand_stream_kernel"}
+
+
+def launches_per_layer(wl: Workload, grouped: bool, path: int, tp: int) -> dict:
+    """Our kernel launches per layer (torch's memsets and NCCL's kernels not counted).
+    path: 1 = one fused launch per call, 3 = streaming shrink + expand pair per
+    call, 2 = shrink + expand per projection."""
     kinds = {name: kind for name, _, _, kind in wl.projs}
     lora = 0
     for grp in GROUPS:
         if tp > 1 and kinds[grp[0]] == ROW:
             lora += 2 * len(grp)  # shrink (fp32 partials) + expand
+        elif path == 2:
+            lora += 2 * len(grp)
         else:
             calls = 1 if grouped else len(grp)
-            lora += calls * (1 if fused else 2)
+            lora += calls * (1 if path == 1 else 2)
     return {"lora": lora, "rmsnorm": 2}
 
 
@@ -419,8 +428,8 @@ def main() -> None:
     step_graph = capture(lambda: run_step(wl, layers, be, grouped=grouped, tp=tp, tp_rank=rank))
     graphs.append(step_graph)
     be.apply_lora(layers[0].x["q"], layers[0].A["q"], layers[0].B["q"], layers[0].y["q"].clone())
-    fused = _native.capi().mlora_last_apply_path() == 1
-    per_layer = launches_per_layer(wl, grouped, fused, tp)
+    path = _native.capi().mlora_last_apply_path()
+    per_layer = launches_per_layer(wl, grouped, path, tp)
     launches_per_step = wl.layers * (per_layer["lora"] + per_layer["rmsnorm"])
 
     for _ in range(args.warmup):
@@ -472,7 +481,7 @@ def main() -> None:
     if tp > 1:
         kernel = "lora part per rank: apply_fused_kernel (column) + shrink/expand + NCCL all-reduce (row)"
     else:
-        kernel = "apply_fused_kernel" if fused else "shrink_kernel+expand_kernel"
+        kernel = APPLY_KERNELS.get(path, "unknown")
     traffic = read_traffic().get(kernel) if wl.name == "cfg2" and tp == 1 else None
     step_bytes = ab["lora"] + ab["rmsnorm"]
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
@@ -526,7 +535,8 @@ def main() -> None:
                "data": "synthetic (seeded; random-init adapters of the named shapes)",
                "config": config_block(wl, n), "roofline": roofline, "step_roofline": step_roofline,
                "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
-               "clocks": clk, "pdl": _native.get_pdl(), "grouped": grouped, "fused_path": fused}
+               "clocks": clk, "pdl": _native.get_pdl(), "grouped": grouped,
+               "apply_path": APPLY_PATH_NAMES.get(path, str(path))}
         print(json.dumps(out), flush=True)
     # graphs that hold NCCL calls go before the process group
     del step_graph, g_lora, g_rms

@@ -70,7 +70,12 @@ CAPI_SIGNATURES = {
     "mlora_last_error": (ctypes.c_char_p, []),
     "mlora_version": (ctypes.c_int, []),
     "mlora_last_apply_path": (ctypes.c_int, []),
+    "mlora_set_apply_path": (None, [ctypes.c_int]),
+    "mlora_get_apply_path": (ctypes.c_int, []),
 }
+
+# mlora_set_apply_path codes
+APPLY_PATHS = {"auto": 0, "fused": 1, "split": 2, "stream": 3}
 
 
 def capi() -> ctypes.CDLL:
@@ -122,6 +127,16 @@ def set_pdl(enable: bool) -> None:
 
 def get_pdl() -> bool:
     return bool(capi().mlora_get_pdl())
+
+
+def set_apply_path(name: str) -> None:
+    """Force the apply_lora path tried first: "auto", "fused", "split" or "stream"."""
+    capi().mlora_set_apply_path(APPLY_PATHS[name])
+
+
+def get_apply_path() -> str:
+    code = capi().mlora_get_apply_path()
+    return next(k for k, v in APPLY_PATHS.items() if v == code)
 
 
 def stream_handle(stream: torch.cuda.Stream | None = None) -> int:

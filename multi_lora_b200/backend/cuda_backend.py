@@ -30,6 +30,7 @@ class CudaLoRABackend(LoRABackend):
         self.stack_num = stack_num
         self._ops = _native.ops()
         self._status: Optional[torch.Tensor] = None
+        self._gmid = torch.empty((0, 0))
 
     # -- routing-error status word ------------------------------------------
     def status_word(self, device: torch.device) -> torch.Tensor:
@@ -57,6 +58,16 @@ class CudaLoRABackend(LoRABackend):
             if bits & 16:
                 names.append("an asynchronous copy did not complete in time")
             raise RuntimeError("mlora: invalid routing metadata: " + "; ".join(names))
+
+    def group_mid_buffer(self, rows: int, max_rank: int, like: torch.Tensor) -> torch.Tensor:
+        """Resident (rows, 4 * max_rank) intermediate for ``apply_lora_group``:
+        projection m's shrink output sits in columns [m*max_rank, (m+1)*max_rank).
+        Reused while it fits (CUDA-graph safe once sized)."""
+        m = self._gmid
+        if (m.shape[0] < rows or m.shape[1] != 4 * max_rank or m.device != like.device
+                or m.dtype != like.dtype):
+            self._gmid = torch.empty((rows, 4 * max_rank), dtype=like.dtype, device=like.device)
+        return self._gmid[:rows]
 
     def _meta(self) -> KernelInputMetaData:
         meta = self.kernel_input_metadata
@@ -112,7 +123,7 @@ class CudaLoRABackend(LoRABackend):
         x = self._check_x(x, "x")
         outs = list(base_outputs)
         targets = [o if (o.dim() == 2 and o.stride(1) == 1) else o.contiguous() for o in outs]
-        mid = self.mid_buffer(x.shape[0], a_stacks[0].shape[-2], x)
+        mid = self.group_mid_buffer(x.shape[0], a_stacks[0].shape[-2], x)
         self._ops.apply_lora_group(
             x, [a.contiguous() for a in a_stacks], [b.contiguous() for b in b_stacks], _i32(meta.seg_lens),
             _i32(meta.seg_indptr), _i32(meta.weight_indices), _i32(meta.lora_ranks), meta.scalings, int(meta.bs),

@@ -1,0 +1,581 @@
+// Streaming apply_lora for decode-sized batches: shrink and expand as two
+// persistent, warp-specialised kernels chained by programmatic dependent launch.
+//
+// Semantics are those of LoRABackend.apply_lora (backend/base.py:60-89 of the
+// reference): mid = T(x @ A[slot, :rank].T) with fp32 accumulation
+// (sgemm_lora_a.py:119-183), then
+// y = T(T(scaling * mid @ B[slot, :, :rank].T) + y) (sgemm_lora_b.py:94-153),
+// for up to four projections that share x and the routing.
+//
+// Work decomposition. Every CTA rebuilds the batch's slot -> token lists from
+// the routing tables in shared memory (a counting sort; slots of rank 0 or
+// with no tokens drop out) and cuts each slot's tokens into tiles of up to
+// kStreamTM rows. Items are then dealt round-robin to one CTA per SM:
+//   shrink kernel: item = (tile, projection); it streams A[slot, :rank, :] and
+//     the tile's x rows through the shared-memory ring in chunks of KC input
+//     columns and accumulates mid for the tile over the whole input dim, so
+//     the reduction is inside one CTA (fixed order, no atomics, no scratch);
+//     the rounded mid rows go to the caller's mid buffer (columns < rank).
+//   expand kernel: item = (tile, projection, OC-row block of B); it streams
+//     B[slot, block, :], the tile's y rows (block columns) and mid rows, and
+//     writes the updated y rows back with one bulk store per row.
+// One producer warp fills a kStreamStages-deep shared-memory ring with 1-D
+// TMA bulk copies (lane 0 arms the stage's full mbarrier with the byte count,
+// the lanes issue one row copy each: a single issuing thread was measured at
+// ~75-100 ns per bulk copy, too slow for row-sized pieces); four consumer
+// warps run mma.sync m16n8k16 tiles and release stages on empty mbarriers.
+// The weights of the first ring fills are requested BEFORE griddepcontrol.wait,
+// so under programmatic dependent launch they stream while the previous
+// kernel finishes; x, y and mid are only read after the wait. The expand
+// kernel is launched right behind the shrink kernel and prefetches its B
+// blocks while the shrink runs; its wait is the shrink -> expand dependency.
+// Each CTA needs ~100 KB of shared memory, so a shrink CTA and an expand CTA
+// share an SM. Every mbarrier wait is bounded (status bit on timeout).
+#include <cstdlib>
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "mma.cuh"
+#include "tma.cuh"
+
+namespace mlora {
+
+constexpr int kStreamConsumers = 4;                          // consumer warps
+constexpr int kStreamThreads = (kStreamConsumers + 1) * 32;  // + one producer warp
+constexpr int kStreamTM = 8;                                 // tokens per tile
+constexpr int kStreamStages = 4;
+
+// Input columns per shrink chunk and B rows per expand block: ~16 KB of
+// weights per ring stage at every rank.
+__host__ __device__ constexpr int stream_kc(int rm) { return 8192 / rm; }
+
+__host__ __device__ constexpr int align128(int b) { return (b + 127) / 128 * 128; }
+
+template <int RM>
+struct ShrinkStage {
+  static constexpr int KC = stream_kc(RM);
+  static constexpr int KCP = KC + 8;  // padded row (odd number of 16-byte units: ldmatrix conflict-free)
+  static constexpr int A_BYTES = align128(RM * KCP * 2);
+  static constexpr int X_BYTES = align128(kStreamTM * KCP * 2);
+  static constexpr int BYTES = A_BYTES + X_BYTES;
+};
+
+template <int RM>
+struct ExpandStage {
+  static constexpr int OC = stream_kc(RM);
+  static constexpr int OCP = OC + 8;
+  static constexpr int MP = RM + 8;
+  static constexpr int B_BYTES = align128(OC * RM * 2 + 16);  // + slack: a half k-step may read 16 B past the block
+  static constexpr int Y_BYTES = align128(kStreamTM * OCP * 2);
+  static constexpr int M_BYTES = align128(kStreamTM * MP * 2);
+  static constexpr int BYTES = B_BYTES + Y_BYTES + M_BYTES;
+};
+
+// Routing arrays in dynamic shared memory behind the ring.
+struct StreamRouting {
+  int* cnt;     // [num_slots] tokens routed to the slot (0 if unused or rank 0)
+  int* fill;    // [num_slots] counting-sort cursor
+  int* off;     // [num_slots] first entry of the slot in tok
+  int* toff;    // [num_slots + 1] first tile of the slot; toff[num_slots] = tiles
+  int* rank;    // [num_slots] rank clamped to [0, R]
+  float* scale; // [num_slots]
+  int* tok;     // [S] token rows grouped by slot
+};
+
+__host__ __device__ inline int stream_routing_bytes(int num_slots, int S) {
+  return 4 * (6 * num_slots + 1 + S);
+}
+
+__device__ __forceinline__ StreamRouting stream_routing(unsigned char* base, int num_slots) {
+  StreamRouting r;
+  int* p = reinterpret_cast<int*>(base);
+  r.cnt = p;
+  r.fill = p + num_slots;
+  r.off = p + 2 * num_slots;
+  r.rank = p + 3 * num_slots;
+  r.scale = reinterpret_cast<float*>(p + 4 * num_slots);
+  r.toff = p + 5 * num_slots;
+  r.tok = p + 6 * num_slots + 1;
+  return r;
+}
+
+// Counting sort of the batch's tokens by slot (every thread of the CTA).
+// Reads only routing tables and ranks/scalings, which no kernel of the step writes.
+__device__ void stream_build_routing(const StreamArgs& p, const StreamRouting& rt, bool want_scale) {
+  __shared__ int s_overflow;
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const bool reporter = blockIdx.x == 0;
+  for (int s = tid; s < p.num_slots; s += nt) {
+    int r = __ldg(p.lora_ranks + s);
+    if (r < 0 || r > p.R) {
+      if (reporter) flag_error(p.status, kErrRankRange);
+      r = r < 0 ? 0 : p.R;
+    }
+    rt.rank[s] = r;
+    rt.cnt[s] = 0;
+    rt.fill[s] = 0;
+    if (want_scale) {
+      float sc;
+      switch (p.scalings_dtype) {
+        case kBF16: sc = __bfloat162float(__ldg(static_cast<const __nv_bfloat16*>(p.scalings) + s)); break;
+        case kF16: sc = __half2float(__ldg(static_cast<const __half*>(p.scalings) + s)); break;
+        default: sc = __ldg(static_cast<const float*>(p.scalings) + s); break;
+      }
+      rt.scale[s] = sc;
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < p.bs; i += nt) {
+    const int w = __ldg(p.weight_indices + i);
+    const int st = __ldg(p.seg_indptr + i), en = __ldg(p.seg_indptr + i + 1);
+    if (w < 0 || w >= p.num_slots) {
+      if (reporter) flag_error(p.status, kErrSlotRange);
+      continue;
+    }
+    if (st < 0 || en < st || en > p.S) {
+      if (reporter) flag_error(p.status, kErrIndptr);
+      continue;
+    }
+    if (en > st && rt.rank[w] > 0) atomicAdd(&rt.cnt[w], en - st);
+  }
+  __syncthreads();
+  if (tid < 32) {  // exclusive scans: token offsets and tile offsets per slot
+    int tok_base = 0, tile_base = 0;
+    for (int s0 = 0; s0 < p.num_slots; s0 += 32) {
+      const int s = s0 + tid;
+      const int c = s < p.num_slots ? rt.cnt[s] : 0;
+      const int t = (c + kStreamTM - 1) / kStreamTM;
+      int ic = c, it = t;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int vc = __shfl_up_sync(0xffffffffu, ic, o);
+        const int vt = __shfl_up_sync(0xffffffffu, it, o);
+        if (tid >= o) {
+          ic += vc;
+          it += vt;
+        }
+      }
+      if (s < p.num_slots) {
+        rt.off[s] = tok_base + ic - c;
+        rt.toff[s] = tile_base + it - t;
+      }
+      tok_base += __shfl_sync(0xffffffffu, ic, 31);
+      tile_base += __shfl_sync(0xffffffffu, it, 31);
+    }
+    if (tid == 0) {
+      // valid routing covers each row at most once; more rows than S means
+      // overlapping segments: flag it and do no work (the token list holds S rows)
+      s_overflow = tok_base > p.S;
+      if (s_overflow) flag_error(p.status, kErrIndptr);
+      rt.toff[p.num_slots] = s_overflow ? 0 : tile_base;
+    }
+  }
+  __syncthreads();
+  if (s_overflow) return;
+  for (int i = tid; i < p.bs; i += nt) {
+    const int w = __ldg(p.weight_indices + i);
+    const int st = __ldg(p.seg_indptr + i), en = __ldg(p.seg_indptr + i + 1);
+    if (w < 0 || w >= p.num_slots || st < 0 || en < st || en > p.S || rt.rank[w] == 0) continue;
+    for (int row = st; row < en; ++row) rt.tok[rt.off[w] + atomicAdd(&rt.fill[w], 1)] = row;
+  }
+  __syncthreads();
+}
+
+struct StreamTile {
+  int slot, start, nt, rank;
+};
+
+// Tile index -> slot (binary search over the tile offsets), first token entry and row count.
+__device__ __forceinline__ StreamTile stream_tile(const StreamRouting& rt, int num_slots, int tile) {
+  int lo = 0, hi = num_slots - 1;
+  while (lo < hi) {  // last slot whose first tile <= tile
+    const int mid = (lo + hi + 1) >> 1;
+    if (rt.toff[mid] <= tile) lo = mid; else hi = mid - 1;
+  }
+  StreamTile t;  // (slots without tiles share their toff with a later slot, so the last match owns `tile`)
+  t.slot = lo;
+  const int k = tile - rt.toff[lo];
+  t.start = rt.off[lo] + k * kStreamTM;
+  t.nt = min(kStreamTM, rt.cnt[lo] - k * kStreamTM);
+  t.rank = rt.rank[lo];
+  return t;
+}
+
+// ---------------------------------------------------------------------------
+// shared pieces of the two kernels
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ StreamModule stream_module(const StreamArgs& p, int m) {
+  StreamModule r = p.mod[0];
+#pragma unroll
+  for (int i = 1; i < kMaxStreamModules; ++i)
+    if (i == m) r = p.mod[i];
+  return r;
+}
+
+// ---------------------------------------------------------------------------
+// shrink
+// ---------------------------------------------------------------------------
+template <typename T, int RM>
+__global__ void __launch_bounds__(kStreamThreads) lora_shrink_stream_kernel(const StreamArgs p) {
+  using SS = ShrinkStage<RM>;
+  constexpr int NC = kStreamConsumers, NS = kStreamStages, TM = kStreamTM;
+  constexpr int KC = SS::KC, KCP = SS::KCP;
+  extern __shared__ __align__(128) unsigned char s_dyn[];
+  __shared__ __align__(8) uint64_t full[NS], empty[NS];
+  __shared__ __align__(16) float s_red[NC][TM][RM];
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const StreamRouting rt = stream_routing(s_dyn + NS * SS::BYTES, p.num_slots);
+  stream_build_routing(p, rt, false);
+  const int tiles = rt.toff[p.num_slots];
+  const int n_items = tiles * p.n_mod;
+  const int G = gridDim.x;
+  const int my_items = blockIdx.x < n_items ? (n_items - 1 - blockIdx.x) / G + 1 : 0;
+  if (my_items == 0) {
+    pdl_trigger();
+    return;
+  }
+  if (tid == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NC);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  pdl_trigger();  // the expand kernel may launch now and prefetch its weights
+
+  const int nch = (p.in_dim + KC - 1) / KC;
+  const int total = my_items * nch;  // ring fills of this CTA
+  if (warp == NC) {
+    // ---------------- producer warp: lane 0 arms the stage, every lane issues copies ----------------
+    auto stage_a = [&](int s) { return reinterpret_cast<T*>(s_dyn + s * SS::BYTES); };
+    auto stage_x = [&](int s) { return reinterpret_cast<T*>(s_dyn + s * SS::BYTES + SS::A_BYTES); };
+    auto issue_a = [&](int f) {
+      const int s = f % NS;
+      const int item = blockIdx.x + (f / nch) * G, c = f % nch;
+      const StreamTile t = stream_tile(rt, p.num_slots, item / p.n_mod);
+      const int k0 = c * KC, kcl = min(KC, p.in_dim - k0);
+      if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(t.rank + t.nt) * kcl * sizeof(T));
+      __syncwarp();
+      const T* a = static_cast<const T*>(stream_module(p, item % p.n_mod).a) + ((int64_t)t.slot * p.R) * p.in_dim + k0;
+      for (int n = lane; n < t.rank; n += 32)
+        bulk_copy_g2s(stage_a(s) + n * KCP, a + (int64_t)n * p.in_dim, kcl * sizeof(T), &full[s]);
+    };
+    auto issue_x = [&](int f) {
+      const int s = f % NS;
+      const int item = blockIdx.x + (f / nch) * G, c = f % nch;
+      const StreamTile t = stream_tile(rt, p.num_slots, item / p.n_mod);
+      const int k0 = c * KC, kcl = min(KC, p.in_dim - k0);
+      const T* x = static_cast<const T*>(p.x) + k0;
+      for (int r = lane; r < t.nt; r += 32)
+        bulk_copy_g2s(stage_x(s) + r * KCP, x + (int64_t)rt.tok[t.start + r] * p.x_stride, kcl * sizeof(T),
+                      &full[s]);
+    };
+    const int pre = min(NS, total);
+    for (int f = 0; f < pre; ++f) issue_a(f);  // weights: before the wait
+    pdl_wait();                                 // x comes from earlier kernels
+    for (int f = 0; f < pre; ++f) issue_x(f);
+    for (int f = pre; f < total; ++f) {
+      if (!mbar_wait(&empty[f % NS], ((f / NS) - 1) & 1, p.status)) break;
+      issue_a(f);
+      issue_x(f);
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  const int ctid = tid;  // 0 .. NC*32-1
+  const int g = lane >> 2, cq = lane & 3;
+  bool ok = true;
+  int f = 0;
+  for (int j = 0; j < my_items; ++j) {
+    const int item = blockIdx.x + j * G;
+    const int m = item % p.n_mod;
+    const StreamTile t = stream_tile(rt, p.num_slots, item / p.n_mod);
+    float acc[RM / 8][4];
+#pragma unroll
+    for (int i = 0; i < RM / 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+    const int xrow = (lane & 15) < t.nt ? (lane & 15) : 0;  // MMA rows past the tile repeat row 0
+    const int brow = lane & 7, bhalf = (lane >> 3) & 1;
+    for (int c = 0; c < nch; ++c, ++f) {
+      const int s = f % NS;
+      if (ok) ok = mbar_wait(&full[s], (f / NS) & 1, p.status);  // after a timeout: no more waits
+      if (ok) {
+        const int ksteps = min(KC, p.in_dim - c * KC) / 16;
+        const uint32_t xa = smem_addr(s_dyn + s * SS::BYTES + SS::A_BYTES) + (uint32_t)(xrow * KCP + (lane >> 4) * 8) * 2u;
+        const uint32_t aa = smem_addr(s_dyn + s * SS::BYTES);
+        for (int kk = warp; kk < ksteps; kk += NC) {
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4(xa + (uint32_t)kk * 32u, a0, a1, a2, a3);
+#pragma unroll
+          for (int i = 0; i < RM / 8; ++i) {
+            if (i * 8 < t.rank) {
+              uint32_t b0, b1;
+              ldsm_x2(aa + (uint32_t)((i * 8 + brow) * KCP + kk * 16 + bhalf * 8) * 2u, b0, b1);
+              mma_16816<T>(acc[i], a0, a1, a2, a3, b0, b1);
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    // cross-warp reduction in warp order, one rounding to T, rows of this tile only
+#pragma unroll
+    for (int i = 0; i < RM / 8; ++i) {
+      s_red[warp][g][i * 8 + 2 * cq] = acc[i][0];
+      s_red[warp][g][i * 8 + 2 * cq + 1] = acc[i][1];
+    }
+    named_barrier(1, NC * 32);
+    if (ok) {
+      T* mid = static_cast<T*>(p.mid) + m * p.R;
+      for (int e = ctid; e < t.nt * t.rank; e += NC * 32) {
+        const int r = e / t.rank, k = e - r * t.rank;
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < NC; ++w) v += s_red[w][r][k];
+        mid[(int64_t)rt.tok[t.start + r] * p.mid_stride + k] = Num<T>::from_f(v);
+      }
+    }
+    named_barrier(1, NC * 32);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// expand
+// ---------------------------------------------------------------------------
+template <typename T, int RM>
+__global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(const StreamArgs p) {
+  using ES = ExpandStage<RM>;
+  constexpr int NC = kStreamConsumers, NS = kStreamStages;
+  constexpr int OC = ES::OC, OCP = ES::OCP, MP = ES::MP;
+  extern __shared__ __align__(128) unsigned char s_dyn[];
+  __shared__ __align__(8) uint64_t full[NS], empty[NS];
+  __shared__ int s_blocks[kMaxStreamModules + 1];  // prefix of OC blocks over the projections
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const StreamRouting rt = stream_routing(s_dyn + NS * ES::BYTES, p.num_slots);
+  if (tid == 0) {
+    int acc = 0;
+    for (int m = 0; m < p.n_mod; ++m) {
+      s_blocks[m] = acc;
+      acc += (stream_module(p, m).out_dim + OC - 1) / OC;
+    }
+    s_blocks[p.n_mod] = acc;
+  }
+  stream_build_routing(p, rt, true);
+  const int per_tile = s_blocks[p.n_mod];
+  const int n_items = rt.toff[p.num_slots] * per_tile;
+  const int G = gridDim.x;
+  const int my_items = blockIdx.x < n_items ? (n_items - 1 - blockIdx.x) / G + 1 : 0;
+  if (my_items == 0) {
+    pdl_trigger();
+    return;
+  }
+  if (tid == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NC);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  pdl_trigger();
+
+  struct Item {
+    StreamTile t;
+    StreamModule m;
+    int mi, o0, ocl;
+  };
+  auto decode = [&](int j) {
+    const int item = blockIdx.x + j * G;
+    Item it;
+    it.t = stream_tile(rt, p.num_slots, item / per_tile);
+    const int r = item % per_tile;
+    int m = 0;
+    while (m + 1 < p.n_mod && s_blocks[m + 1] <= r) ++m;
+    it.mi = m;
+    it.m = stream_module(p, m);
+    it.o0 = (r - s_blocks[m]) * OC;
+    it.ocl = min(OC, it.m.out_dim - it.o0);
+    return it;
+  };
+  auto stage_b = [&](int s) { return reinterpret_cast<T*>(s_dyn + s * ES::BYTES); };
+  auto stage_y = [&](int s) { return reinterpret_cast<T*>(s_dyn + s * ES::BYTES + ES::B_BYTES); };
+  auto stage_m = [&](int s) { return reinterpret_cast<T*>(s_dyn + s * ES::BYTES + ES::B_BYTES + ES::Y_BYTES); };
+
+  if (warp == NC) {
+    // ---------------- producer warp: lane 0 arms the stage, every lane issues copies ----------------
+    auto issue_b = [&](int j) {
+      const int s = j % NS;
+      const Item it = decode(j);
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&full[s], (uint32_t)(it.ocl * p.R + it.t.nt * it.ocl + it.t.nt * p.R) * sizeof(T));
+        const T* b = static_cast<const T*>(it.m.b) + ((int64_t)it.t.slot * it.m.out_dim + it.o0) * p.R;
+        bulk_copy_g2s(stage_b(s), b, (uint32_t)it.ocl * p.R * sizeof(T), &full[s]);
+      }
+      __syncwarp();
+    };
+    auto issue_ym = [&](int j) {
+      const int s = j % NS;
+      const Item it = decode(j);
+      const T* y = static_cast<const T*>(it.m.y) + it.o0;
+      const T* mid = static_cast<const T*>(p.mid) + it.mi * p.R;
+      for (int r = lane; r < 2 * it.t.nt; r += 32) {
+        const int t = r >> 1;
+        const int64_t row = rt.tok[it.t.start + t];
+        if ((r & 1) == 0) bulk_copy_g2s(stage_y(s) + t * OCP, y + row * it.m.y_stride, it.ocl * sizeof(T), &full[s]);
+        else bulk_copy_g2s(stage_m(s) + t * MP, mid + row * p.mid_stride, p.R * sizeof(T), &full[s]);
+      }
+    };
+    const int pre = min(NS, my_items);
+    for (int j = 0; j < pre; ++j) issue_b(j);  // adapter weights: before the wait
+    pdl_wait();                                 // mid (shrink kernel) and y (base projection)
+    for (int j = 0; j < pre; ++j) issue_ym(j);
+    for (int j = pre; j < my_items; ++j) {
+      if (!mbar_wait(&empty[j % NS], ((j / NS) - 1) & 1, p.status)) break;
+      issue_b(j);
+      issue_ym(j);
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  const int g = lane >> 2, cq = lane & 3;
+  const int brow = lane & 7, bhalf = (lane >> 3) & 1;
+  bool ok = true;
+  for (int j = 0; j < my_items; ++j) {
+    const int s = j % NS;
+    const Item it = decode(j);
+    if (ok) ok = mbar_wait(&full[s], (j / NS) & 1, p.status);  // after a timeout: no more waits
+    const int rank = it.t.rank, nt = it.t.nt;
+    if (ok) {
+      const float scale = rt.scale[it.t.slot];
+      // A operand: the tile's mid rows; columns >= rank (stale in the caller's buffer) are zeroed in registers
+      uint32_t am[RM / 16][4];
+      const int mrow = (lane & 15) < nt ? (lane & 15) : 0;
+      const uint32_t ma = smem_addr(stage_m(s)) + (uint32_t)(mrow * MP + (lane >> 4) * 8) * 2u;
+#pragma unroll
+      for (int kk = 0; kk < RM / 16; ++kk) {
+        ldsm_x4(ma + (uint32_t)kk * 32u, am[kk][0], am[kk][1], am[kk][2], am[kk][3]);
+        const int c0 = kk * 16 + 2 * cq, c1 = c0 + 8;
+        const uint32_t m0 = (c0 < rank ? 0x0000ffffu : 0u) | (c0 + 1 < rank ? 0xffff0000u : 0u);
+        const uint32_t m1 = (c1 < rank ? 0x0000ffffu : 0u) | (c1 + 1 < rank ? 0xffff0000u : 0u);
+        am[kk][0] &= m0;
+        am[kk][1] &= m0;
+        am[kk][2] &= m1;
+        am[kk][3] &= m1;
+      }
+      const int ksteps = (rank + 15) / 16;
+      const uint32_t ba = smem_addr(stage_b(s));
+      T* ys = stage_y(s);
+      for (int nb = warp; nb < it.ocl / 8; nb += NC) {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int kk = 0; kk < RM / 16; ++kk) {
+          if (kk < ksteps) {
+            uint32_t b0, b1;
+            ldsm_x2(ba + (uint32_t)((nb * 8 + brow) * p.R + kk * 16 + bhalf * 8) * 2u, b0, b1);
+            // B columns >= rank (stale, or past the row when R % 16 == 8) contribute zero
+            const int c0 = kk * 16 + 2 * cq, c1 = c0 + 8;
+            b0 &= (c0 < rank ? 0x0000ffffu : 0u) | (c0 + 1 < rank ? 0xffff0000u : 0u);
+            b1 &= (c1 < rank ? 0x0000ffffu : 0u) | (c1 + 1 < rank ? 0xffff0000u : 0u);
+            mma_16816<T>(acc, am[kk][0], am[kk][1], am[kk][2], am[kk][3], b0, b1);
+          }
+        }
+        if (g < nt) {
+          uint32_t* yp = reinterpret_cast<uint32_t*>(ys + g * OCP + nb * 8 + 2 * cq);
+          const uint32_t u = *yp;
+          *yp = Pack2<T>::pack(Num<T>::from_f(round_to<T>(acc[0] * scale) + Pack2<T>::lo(u)),
+                               Num<T>::from_f(round_to<T>(acc[1] * scale) + Pack2<T>::hi(u)));
+        }
+      }
+    }
+    fence_proxy_async_smem();  // the y tile written above is read next by the bulk stores
+    named_barrier(1, NC * 32);
+    if (tid == 0) {
+      if (ok) {
+        T* y = static_cast<T*>(it.m.y) + it.o0;
+        for (int r = 0; r < nt; ++r)
+          bulk_copy_s2g(y + (int64_t)rt.tok[it.t.start + r] * it.m.y_stride, stage_y(s) + r * OCP,
+                        it.ocl * sizeof(T));
+        bulk_commit();
+        bulk_wait_read_all();  // the stage may be refilled once the stores have read it
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+  if (tid == 0) bulk_wait_all();
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+namespace {
+
+int stream_sm_count() {
+  static int n = [] {
+    int dev = 0, c = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return 148;
+    }
+    return c;
+  }();
+  return n;
+}
+
+template <typename K>
+bool ensure_smem(K kern, int bytes, int& set, std::mutex& mu) {
+  std::lock_guard<std::mutex> lock(mu);
+  if (bytes <= set) return true;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  set = bytes;
+  return true;
+}
+
+template <typename T, int RM>
+cudaError_t launch_stream_rm(const StreamArgs& a, cudaStream_t st, bool pdl) {
+  static std::mutex mu;
+  static int set_s = 0, set_e = 0;
+  const int route = align128(stream_routing_bytes(a.num_slots, a.S));
+  const int smem_s = kStreamStages * ShrinkStage<RM>::BYTES + route;
+  const int smem_e = kStreamStages * ExpandStage<RM>::BYTES + route;
+  auto ks = lora_shrink_stream_kernel<T, RM>;
+  auto ke = lora_expand_stream_kernel<T, RM>;
+  if (!ensure_smem(ks, smem_s, set_s, mu) || !ensure_smem(ke, smem_e, set_e, mu)) return cudaErrorNotSupported;
+  const dim3 grid(stream_sm_count());
+  cudaError_t e = launch_kernel(ks, grid, dim3(kStreamThreads), smem_s, st, pdl, a);
+  if (e != cudaSuccess) return e;
+  // the expand kernel always follows with the programmatic attribute: its wait is the shrink -> expand edge
+  return launch_kernel(ke, grid, dim3(kStreamThreads), smem_e, st, true, a);
+}
+
+}  // namespace
+
+constexpr int kStreamMaxRoutingBytes = 48 * 1024;
+
+// Returns cudaErrorNotSupported when the shape is outside this path (the caller
+// then uses another one).
+cudaError_t launch_apply_stream(const StreamArgs& a, int dtype, cudaStream_t st, bool pdl) {
+  if (dtype != kBF16 && dtype != kF16) return cudaErrorNotSupported;
+  if (a.n_mod < 1 || a.n_mod > kMaxStreamModules || a.R > 64 || a.R % 8 != 0 || a.in_dim % 16 != 0)
+    return cudaErrorNotSupported;
+  if (stream_routing_bytes(a.num_slots, a.S) > kStreamMaxRoutingBytes) return cudaErrorNotSupported;
+  const int rm = a.R <= 16 ? 16 : a.R <= 32 ? 32 : 64;
+  if (dtype == kBF16)
+    return rm == 16 ? launch_stream_rm<__nv_bfloat16, 16>(a, st, pdl)
+         : rm == 32 ? launch_stream_rm<__nv_bfloat16, 32>(a, st, pdl)
+                    : launch_stream_rm<__nv_bfloat16, 64>(a, st, pdl);
+  return rm == 16 ? launch_stream_rm<__half, 16>(a, st, pdl)
+       : rm == 32 ? launch_stream_rm<__half, 32>(a, st, pdl)
+                  : launch_stream_rm<__half, 64>(a, st, pdl);
+}
+
+}  // namespace mlora

@@ -60,6 +60,26 @@ struct Num<float> {
   static __device__ __forceinline__ float from_f(float v) { return v; }
 };
 
+// Two 16-bit elements packed in one 32-bit word (element 0 in the low half).
+template <typename T>
+struct Pack2;
+template <>
+struct Pack2<__nv_bfloat16> {
+  static __device__ __forceinline__ uint32_t pack(__nv_bfloat16 a, __nv_bfloat16 b) {
+    return (uint32_t)__bfloat16_as_ushort(a) | ((uint32_t)__bfloat16_as_ushort(b) << 16);
+  }
+  static __device__ __forceinline__ float lo(uint32_t u) { return __bfloat162float(__ushort_as_bfloat16((unsigned short)(u & 0xffffu))); }
+  static __device__ __forceinline__ float hi(uint32_t u) { return __bfloat162float(__ushort_as_bfloat16((unsigned short)(u >> 16))); }
+};
+template <>
+struct Pack2<__half> {
+  static __device__ __forceinline__ uint32_t pack(__half a, __half b) {
+    return (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
+  }
+  static __device__ __forceinline__ float lo(uint32_t u) { return __half2float(__ushort_as_half((unsigned short)(u & 0xffffu))); }
+  static __device__ __forceinline__ float hi(uint32_t u) { return __half2float(__ushort_as_half((unsigned short)(u >> 16))); }
+};
+
 // Round an fp32 value through element type T and back (the value a tensor of
 // dtype T would hold).
 template <typename T>

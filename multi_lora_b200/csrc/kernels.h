@@ -93,6 +93,32 @@ struct FusedArgs {
 
 cudaError_t launch_apply_fused(FusedArgs a, int dtype, cudaStream_t st, bool pdl);
 
+// Streaming apply (persistent shrink + expand kernels, csrc/apply_stream.cu).
+constexpr int kMaxStreamModules = 4;
+struct StreamModule {
+  const void* a;          // A stack [K, R, in], contiguous
+  const void* b;          // B stack [K, out, R], contiguous
+  void* y;                // [S, out] at y_stride, updated in place
+  int64_t y_stride;
+  int out_dim;
+};
+struct StreamArgs {
+  const void* x;          // [S, in] rows at x_stride elements
+  int64_t x_stride;
+  StreamModule mod[kMaxStreamModules];
+  int n_mod;
+  void* mid;              // [S, >= n_mod * R] at mid_stride: projection m's shrink output in columns [m*R, m*R + rank)
+  int64_t mid_stride;
+  const int32_t* seg_indptr;
+  const int32_t* weight_indices;
+  const int32_t* lora_ranks;
+  const void* scalings;
+  int scalings_dtype;
+  int bs, S, in_dim, R, num_slots;
+  uint32_t* status;
+};
+cudaError_t launch_apply_stream(const StreamArgs& a, int dtype, cudaStream_t st, bool pdl);
+
 // Sets the message mlora_last_error() returns on this thread; returns `code`.
 int report_error(int code, const char* msg);
 cudaError_t launch_shrink(const ShrinkArgs& a, int dtype, bool out_f32, cudaStream_t st, bool pdl);

@@ -145,8 +145,22 @@ def test_random_cases_match_oracle(cuda_dev, dtype, shape):
     _check_case(c, cuda_dev, dtype)
 
 
-def _check_apply(c, dev, dtype, expect_path=None):
-    """apply_lora through the C ABI (fused launch when eligible) against the oracle."""
+class forced_path:
+    """Force the apply path tried first (mlora_set_apply_path) inside a with-block."""
+
+    def __init__(self, name):
+        self.name = name
+
+    def __enter__(self):
+        self.old = _native.get_apply_path()
+        _native.set_apply_path(self.name)
+
+    def __exit__(self, *exc):
+        _native.set_apply_path(self.old)
+
+
+def _check_apply(c, dev, dtype, expect_path=None, force="auto"):
+    """apply_lora through the C ABI (path `force` tried first) against the oracle."""
     S = c["x"].shape[0]
     R = c["A"].shape[1]
     n_out = c["B"].shape[1]
@@ -156,8 +170,9 @@ def _check_apply(c, dev, dtype, expect_path=None):
     p0, p1 = c["pad"]
     y = c["big"][p0:p0 + S, p1:p1 + n_out]
     status = torch.zeros(1, dtype=torch.int32, device=dev)
-    C.check(C.apply_lora(c["x"], c["A"], c["B"], meta, mid, y, status=status))
-    path = _native.capi().mlora_last_apply_path()
+    with forced_path(force):
+        C.check(C.apply_lora(c["x"], c["A"], c["B"], meta, mid, y, status=status))
+        path = _native.capi().mlora_last_apply_path()
     torch.cuda.synchronize()
     assert int(status.item()) == 0
     if expect_path is not None:
@@ -184,6 +199,7 @@ def _check_apply(c, dev, dtype, expect_path=None):
 
 
 FUSED_SHAPES = [s for s in SHAPES if s[0] % 8 == 0 and s[2] % 8 == 0 and s[2] <= 64 and max(s[4]) <= 16]
+STREAM_SHAPES = [s for s in SHAPES if s[0] % 16 == 0 and s[1] % 8 == 0 and s[2] % 8 == 0 and s[2] <= 64]
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
@@ -191,25 +207,91 @@ FUSED_SHAPES = [s for s in SHAPES if s[0] % 8 == 0 and s[2] % 8 == 0 and s[2] <=
 def test_fused_apply_matches_oracle(cuda_dev, dtype, shape):
     n_in, n_out, R, ranks, lens = shape
     c = _case(hash((n_in, n_out, R, 1)) % 1000, dtype, n_in, n_out, R, ranks, lens, cuda_dev)
-    _check_apply(c, cuda_dev, dtype, expect_path=1)
+    _check_apply(c, cuda_dev, dtype, expect_path=1, force="fused")
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", STREAM_SHAPES, ids=lambda s: f"{s[0]}x{s[1]}r{s[2]}")
+def test_stream_apply_matches_oracle(cuda_dev, dtype, shape):
+    """The streaming shrink/expand pair (chosen automatically from 256 rows up)."""
+    n_in, n_out, R, ranks, lens = shape
+    c = _case(hash((n_in, n_out, R, 3)) % 1000, dtype, n_in, n_out, R, ranks, lens, cuda_dev)
+    _check_apply(c, cuda_dev, dtype, expect_path=3, force="stream")
 
 
 @pytest.mark.parametrize("shape", [s for s in SHAPES if s not in FUSED_SHAPES], ids=lambda s: f"{s[0]}x{s[1]}r{s[2]}")
 def test_apply_falls_back_to_two_launches(cuda_dev, shape):
+    """Below 256 rows, shapes the fused kernel cannot take run shrink + expand."""
     n_in, n_out, R, ranks, lens = shape
     c = _case(hash((n_in, n_out, R, 2)) % 1000, torch.bfloat16, n_in, n_out, R, ranks, lens, cuda_dev)
     _check_apply(c, cuda_dev, torch.bfloat16, expect_path=2)
 
 
+@pytest.mark.parametrize("shape", SHAPES[:2] + SHAPES[7:8], ids=lambda s: f"{s[0]}x{s[1]}r{s[2]}")
+def test_forced_split_apply_matches_oracle(cuda_dev, shape):
+    n_in, n_out, R, ranks, lens = shape
+    c = _case(hash((n_in, n_out, R, 4)) % 1000, torch.bfloat16, n_in, n_out, R, ranks, lens, cuda_dev)
+    _check_apply(c, cuda_dev, torch.bfloat16, expect_path=2, force="split")
+
+
 def test_fused_apply_many_segments_and_cluster16(cuda_dev):
     """bs above one scan pass (256) and an in-dim that needs 16-CTA clusters."""
     c = _case(21, torch.bfloat16, 512, 640, 16, [16, 16, 8] * 4, [1] * 700, cuda_dev)
-    _check_apply(c, cuda_dev, torch.bfloat16, expect_path=1)
+    _check_apply(c, cuda_dev, torch.bfloat16, expect_path=1, force="fused")
     c = _case(22, torch.bfloat16, 40960, 1024, 16, [16] * 4, [1] * 16, cuda_dev)
-    _check_apply(c, cuda_dev, torch.bfloat16, expect_path=1)
+    _check_apply(c, cuda_dev, torch.bfloat16, expect_path=1, force="fused")
 
 
-def test_fused_apply_rank0_and_unused_slots_leave_y(cuda_dev):
+def test_stream_apply_many_slots_and_long_segments(cuda_dev):
+    """cfg5-like routing (128 slots, 512 one-token segments), one slot with 100
+    tokens (13 tiles), and more segments than one slot's tile."""
+    c = _case(31, torch.bfloat16, 1024, 512, 16, [16, 8, 0, 16] * 32, [1] * 512, cuda_dev)
+    _check_apply(c, cuda_dev, torch.bfloat16, expect_path=3)
+    c = _case(32, torch.bfloat16, 512, 1024, 32, [32, 24], [100, 3, 1, 60], cuda_dev)
+    _check_apply(c, cuda_dev, torch.bfloat16, expect_path=3, force="stream")
+
+
+def test_stream_apply_is_deterministic(cuda_dev):
+    """Two calls in a row on the same inputs give bit-identical y and mid."""
+    c = _case(33, torch.bfloat16, 4096, 4096, 16, [16] * 32, [1] * 64, cuda_dev, nan_tails=False)
+    meta = C.make_meta(c["lens"], c["widx"], c["ranks"], c["scal"], cuda_dev)
+    outs = []
+    with forced_path("stream"):
+        for _ in range(2):
+            mid = torch.zeros(64, 16, dtype=torch.bfloat16, device=cuda_dev)
+            y = c["ybase"].to(cuda_dev).clone()
+            C.check(C.apply_lora(c["x"], c["A"], c["B"], meta, mid, y))
+            assert _native.capi().mlora_last_apply_path() == 3
+            outs.append((mid, y))
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+
+
+def test_stream_apply_invalid_routing_sets_status(cuda_dev):
+    """Slot out of range, overlapping segments (more rows than S) and a rank
+    above max_rank are reported; the launch stays in bounds."""
+    dev = cuda_dev
+    x = torch.randn(4, 64, device=dev).bfloat16()
+    A = torch.randn(2, 16, 64, device=dev).bfloat16()
+    B = torch.randn(2, 128, 16, device=dev).bfloat16()
+    cases = {
+        1: C.make_meta([1, 1], [0, 5], [16, 16], [1.0, 1.0], dev),
+        4: C.make_meta([4, 3, 3], [0, 1, 0], [16, 16], [1.0, 1.0], dev, indptr=[0, 4, 1, 4]),
+        2: C.make_meta([1, 1], [0, 1], [16, 99], [1.0, 1.0], dev),
+    }
+    for bit, meta in cases.items():
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        mid = torch.zeros(4, 16, dtype=torch.bfloat16, device=dev)
+        y = torch.zeros(4, 128, dtype=torch.bfloat16, device=dev)
+        with forced_path("stream"):
+            C.check(C.apply_lora(x, A, B, meta, mid, y, status=status))
+            assert _native.capi().mlora_last_apply_path() == 3
+        torch.cuda.synchronize()
+        assert int(status.item()) & bit, (bit, int(status.item()))
+
+
+@pytest.mark.parametrize("force", ["fused", "stream"])
+def test_apply_rank0_and_unused_slots_leave_y(cuda_dev, force):
     """Only base-model (rank 0) segments: y is bit-identical afterwards."""
     c = _case(23, torch.bfloat16, 1024, 512, 16, [0, 16, 16], [1] * 8, cuda_dev, nan_tails=False)
     c["widx"] = [0] * 8
@@ -217,18 +299,22 @@ def test_fused_apply_rank0_and_unused_slots_leave_y(cuda_dev):
     meta = C.make_meta(c["lens"], c["widx"], c["ranks"], c["scal"], cuda_dev)
     mid = torch.zeros(8, 16, dtype=torch.bfloat16, device=cuda_dev)
     p0, p1 = c["pad"]
-    C.check(C.apply_lora(c["x"], c["A"], c["B"], meta, mid, c["big"][p0:p0 + 8, p1:p1 + 512]))
+    with forced_path(force):
+        C.check(C.apply_lora(c["x"], c["A"], c["B"], meta, mid, c["big"][p0:p0 + 8, p1:p1 + 512]))
     torch.cuda.synchronize()
     assert torch.equal(c["big"], before)
 
 
-@pytest.mark.parametrize("outs, R, ranks, lens, path", [
-    ((4096, 1024, 1024), 16, [16] * 8, [1] * 32, 1),        # q/k/v of a GQA block
-    ((11008, 11008), 16, [16, 0, 16, 8], [1] * 24, 1),      # gate/up
-    ((384, 200, 72), 64, [64, 8, 17], [3, 1, 5, 2], 1),     # mixed ranks, out % 8 != 0 for two
-    ((96, 64), 20, [20, 4], [2, 1, 3], 2),                  # R % 8 != 0: two launches per projection
+@pytest.mark.parametrize("outs, R, ranks, lens, path, wide_path", [
+    ((4096, 1024, 1024), 16, [16] * 8, [1] * 32, 1, 3),        # q/k/v of a GQA block
+    ((11008, 11008), 16, [16, 0, 16, 8], [1] * 24, 1, 3),      # gate/up
+    ((384, 200, 72), 64, [64, 8, 17], [3, 1, 5, 2], 1, 3),     # mixed ranks
+    ((96, 64), 20, [20, 4], [2, 1, 3], 2, 2),                  # R % 8 != 0: two launches per projection
 ])
-def test_group_matches_separate_projections(cuda_dev, outs, R, ranks, lens, path):
+@pytest.mark.parametrize("wide", [False, True], ids=["auto_mid_R", "stream_mid_4R"])
+def test_group_matches_separate_projections(cuda_dev, outs, R, ranks, lens, path, wide_path, wide):
+    """Automatic path with mid [S, R]; the streaming pair (forced) needs mid
+    [S, >= n*R], one column block per projection."""
     """mlora_apply_lora_group == one oracle apply per projection (shared x and routing)."""
     import ctypes
 
@@ -254,17 +340,20 @@ def test_group_matches_separate_projections(cuda_dev, outs, R, ranks, lens, path
         y0.append(yb)
         ys.append(yb.to(dev).clone())
     xd = x.to(dev)
-    mid = torch.zeros(S, R, dtype=dt, device=dev)
+    mid_cols = 4 * R if wide else R
+    mid = torch.zeros(S, mid_cols, dtype=dt, device=dev)
     n = len(outs)
     P = ctypes.c_void_p
     arr = lambda vals, t: (t * n)(*vals)  # noqa: E731
     m = meta.struct()
-    rc = _native.capi().mlora_apply_lora_group(
-        xd.data_ptr(), S, n_in, n_in, n, arr([a.data_ptr() for a in As], P), arr([b.data_ptr() for b in Bs], P),
-        arr(list(outs), ctypes.c_int64), arr([y.data_ptr() for y in ys], P), arr([y.stride(0) for y in ys], ctypes.c_int64),
-        R, ctypes.byref(m), mid.data_ptr(), R, 0, None, torch.cuda.current_stream().cuda_stream)
-    C.check(rc)
-    assert _native.capi().mlora_last_apply_path() == path
+    with forced_path("stream" if wide else "auto"):
+        rc = _native.capi().mlora_apply_lora_group(
+            xd.data_ptr(), S, n_in, n_in, n, arr([a.data_ptr() for a in As], P), arr([b.data_ptr() for b in Bs], P),
+            arr(list(outs), ctypes.c_int64), arr([y.data_ptr() for y in ys], P),
+            arr([y.stride(0) for y in ys], ctypes.c_int64), R, ctypes.byref(m), mid.data_ptr(), mid_cols, 0, None,
+            torch.cuda.current_stream().cuda_stream)
+        C.check(rc)
+        assert _native.capi().mlora_last_apply_path() == (wide_path if wide else path)
     torch.cuda.synchronize()
     ind = meta.seg_indptr.cpu().numpy()
     for a, b, yb, y in zip(As, Bs, y0, ys):
@@ -345,18 +434,20 @@ def test_invalid_routing_sets_status_and_skips(cuda_dev):
         assert int(status.item()) & bit, (bit, int(status.item()))
 
 
-def test_pdl_on_and_off_agree(cuda_dev):
+@pytest.mark.parametrize("force", ["fused", "stream"])
+def test_pdl_on_and_off_agree(cuda_dev, force):
     c = _case(13, torch.bfloat16, 4096, 4096, 16, [16] * 8, [1] * 32, cuda_dev, nan_tails=False)
     meta = C.make_meta(c["lens"], c["widx"], c["ranks"], c["scal"], cuda_dev)
     outs = []
     old = _native.get_pdl()
-    for pdl in (True, False):
-        _native.set_pdl(pdl)
-        mid = torch.zeros(32, 16, dtype=torch.bfloat16, device=cuda_dev)
-        y = c["ybase"].to(cuda_dev).clone()
-        C.check(C.apply_lora(c["x"], c["A"], c["B"], meta, mid, y))
-        torch.cuda.synchronize()
-        outs.append(y)
+    with forced_path(force):
+        for pdl in (True, False):
+            _native.set_pdl(pdl)
+            mid = torch.zeros(32, 16, dtype=torch.bfloat16, device=cuda_dev)
+            y = c["ybase"].to(cuda_dev).clone()
+            C.check(C.apply_lora(c["x"], c["A"], c["B"], meta, mid, y))
+            torch.cuda.synchronize()
+            outs.append(y)
     _native.set_pdl(old)
     assert torch.equal(outs[0], outs[1])
 
