@@ -58,8 +58,9 @@ class Workload:
     """A Llama-shaped decode workload: per layer q/k/v/o/gate/up/down LoRA
     projections and two RMSNorms; ``tokens`` tokens with uniform adapter ids."""
 
-    def __init__(self, name, desc, hidden, kv, inter, layers, tokens, adapters, rank, alpha):
+    def __init__(self, name, desc, hidden, kv, inter, layers, tokens, adapters, rank, alpha, requests=None):
         self.name, self.desc = name, desc
+        self.requests = requests  # prefill: number of requests, one adapter each, lengths drawn in routing()
         self.hidden, self.layers, self.tokens = hidden, layers, tokens
         self.adapters, self.rank, self.scaling = adapters, rank, alpha / rank
         # (name, in, out, tensor-parallel kind)
@@ -72,6 +73,9 @@ class Workload:
 WORKLOADS = {
     "cfg2": Workload("cfg2", "Llama-2-7B-shaped decode: 32 layers x 7 LoRA projections + 2 RMSNorm, 64 tokens, "
                              "32 adapters r16 (alpha 32), bf16", 4096, 4096, 11008, 32, 64, 32, 16, 32),
+    "cfg3": Workload("cfg3", "Llama-3-8B-shaped prefill: 32 layers x 7 LoRA projections + 2 RMSNorm, 8 requests of "
+                             "128..1024 tokens (seed 0: 4340 tokens), one adapter each, 8 adapters r64 (alpha 128), "
+                             "bf16", 4096, 1024, 14336, 32, 4340, 8, 64, 128, requests=8),
     "cfg5": Workload("cfg5", "Llama-3-70B-shaped decode: 80 layers x 7 LoRA projections + 2 RMSNorm, 512 tokens, "
                              "128 adapters r16 (alpha 32), bf16", 8192, 1024, 28672, 80, 512, 128, 16, 32),
 }
@@ -81,8 +85,8 @@ def peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return {"hbm_gbs": float(d["hbm_gbs"]), "src": "measured"}
-    return {"hbm_gbs": 6650.0, "src": "fallback"}
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
 
 
 def routing(wl: Workload, seed: int = 0):
@@ -90,8 +94,14 @@ def routing(wl: Workload, seed: int = 0):
     from multi_lora_b200.batch_info import BatchLoRAInfo, group_rows
 
     g = torch.Generator().manual_seed(seed)
-    ids = torch.randint(0, wl.adapters, (wl.tokens,), generator=g).tolist()
-    names, lens = group_rows(ids, [])
+    if wl.requests:  # prefill: request i uses adapter i, lengths uniform in [128, 1024]
+        req_lens = torch.randint(128, 1025, (wl.requests,), generator=g).tolist()
+        ids = [i for i, n in enumerate(req_lens) for _ in range(n)]
+        names, lens = list(range(wl.requests)), req_lens
+        assert sum(lens) == wl.tokens, (sum(lens), wl.tokens)
+    else:
+        ids = torch.randint(0, wl.adapters, (wl.tokens,), generator=g).tolist()
+        names, lens = group_rows(ids, [])
     info = BatchLoRAInfo(weight_indices=list(names), lora_ranks=[wl.rank] * wl.adapters,
                          scalings=[wl.scaling] * wl.adapters)
     return ids, info, lens
@@ -117,12 +127,14 @@ def algorithmic_bytes(wl: Workload, ids, tp: int) -> dict:
     d = len(set(ids))
     T, es, r = wl.tokens, 2, wl.rank
     dims = shard_dims(wl, tp)
-    lora = 0
+    lora = flops = 0
     for name, *_ in wl.projs:
         i, o, _ = dims[name]
         lora += d * r * i * es + d * r * o * es + T * i * es + 2 * T * o * es + 2 * T * r * es
+        flops += 2 * T * r * (i + o)
     rms = 2 * (2 * T * wl.hidden * es + wl.hidden * es)
-    return {"lora": lora * wl.layers, "rmsnorm": rms * wl.layers, "distinct_adapters": d}
+    return {"lora": lora * wl.layers, "rmsnorm": rms * wl.layers, "distinct_adapters": d,
+            "lora_flops": flops * wl.layers}
 
 
 class Layer:
@@ -190,9 +202,10 @@ def run_step(wl: Workload, layers, be, parts=("rmsnorm", "lora"), grouped=True, 
                     be.apply_lora(L.x[n], L.A[n], L.B[n], L.y[n])
 
 
-APPLY_PATH_NAMES = {1: "fused", 2: "split", 3: "stream"}
+APPLY_PATH_NAMES = {1: "fused", 2: "split", 3: "stream", 4: "tc"}
 APPLY_KERNELS = {1: "apply_fused_kernel", 2: "shrink_kernel+expand_kernel",
-                 3: "lora_shrink_stream_kernel+lora_expand_stream_kernel"}
+                 3: "lora_shrink_stream_kernel+lora_expand_stream_kernel",
+                 4: "lora_shrink_tc_kernel+lora_expand_tc_kernel"}
 
 
 def launches_per_layer(wl: Workload, grouped: bool, path: int, tp: int) -> dict:
@@ -487,7 +500,10 @@ def main() -> None:
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                 "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": traffic, "kernel": kernel,
                 "peak_source": pk["src"], "bytes_per_launch": round(per_launch_bytes),
-                "launch_us": round(per_launch_ms * 1e3, 3), "launches_timed": lora_launches}
+                "launch_us": round(per_launch_ms * 1e3, 3), "launches_timed": lora_launches,
+                "tensor": {"achieved_tflops": round(ab["lora_flops"] / (lora_ms / 1e3) / 1e12, 2),
+                           "peak_tflops": pk["bf16_tflops"],
+                           "frac": round(ab["lora_flops"] / (lora_ms / 1e3) / 1e12 / pk["bf16_tflops"], 4)}}
     step_achieved = step_bytes / (ms / 1e3) / 1e9
     step_roofline = {"bytes_per_step": step_bytes, "achieved": round(step_achieved, 1),
                      "frac": round(step_achieved / pk["hbm_gbs"], 4), "unit": "GB/s",

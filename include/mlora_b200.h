@@ -209,14 +209,16 @@ int mlora_version(void);
 
 /* Diagnostics: which path the last mlora_apply_lora on this thread took
  * (1 = one fused launch, 2 = shrink + expand launches, 3 = the streaming
- * shrink/expand kernel pair, 0 = none yet). */
+ * shrink/expand kernel pair, 4 = the tensor-core (tcgen05) shrink/expand pair
+ * for long segments, 0 = none yet). */
 int mlora_last_apply_path(void);
 
 /* Tuning and tests: force the path mlora_apply_lora / mlora_apply_lora_group
  * try first (0 = automatic, 1 = fused, 2 = shrink + expand, 3 = streaming
- * pair). A shape the forced path cannot take falls through stream -> fused ->
- * shrink + expand. Process-wide; the environment variable MLORA_APPLY_PATH
- * (fused | split | stream) sets the initial value. No reference counterpart. */
+ * pair, 4 = tensor-core pair). A shape the forced path cannot take falls
+ * through tensor-core -> stream -> fused -> shrink + expand. Process-wide; the
+ * environment variable MLORA_APPLY_PATH (fused | split | stream | tc) sets the
+ * initial value. No reference counterpart. */
 void mlora_set_apply_path(int path);
 int mlora_get_apply_path(void);
 

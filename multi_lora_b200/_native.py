@@ -75,7 +75,7 @@ CAPI_SIGNATURES = {
 }
 
 # mlora_set_apply_path codes
-APPLY_PATHS = {"auto": 0, "fused": 1, "split": 2, "stream": 3}
+APPLY_PATHS = {"auto": 0, "fused": 1, "split": 2, "stream": 3, "tc": 4}
 
 
 def capi() -> ctypes.CDLL:
@@ -130,7 +130,7 @@ def get_pdl() -> bool:
 
 
 def set_apply_path(name: str) -> None:
-    """Force the apply_lora path tried first: "auto", "fused", "split" or "stream"."""
+    """Force the apply_lora path tried first: "auto", "fused", "split", "stream" or "tc"."""
     capi().mlora_set_apply_path(APPLY_PATHS[name])
 
 

@@ -12,18 +12,18 @@
 namespace {
 
 thread_local char g_err[512] = {0};
-thread_local int g_last_apply_path = 0;  // 1 fused launch, 2 shrink + expand, 3 streaming pair
+thread_local int g_last_apply_path = 0;  // 1 fused, 2 shrink + expand, 3 streaming pair, 4 tensor-core pair
 int g_pdl = -1;  // -1: not read from the environment yet
 
-// apply_lora path choice: 0 = automatic; MLORA_APPLY_PATH=fused|split|stream
+// apply_lora path choice: 0 = automatic; MLORA_APPLY_PATH=fused|split|stream|tc
 // forces one (tuning and tests; a forced path the shape does not fit falls
-// through to the next one: stream -> fused -> split).
+// through to the next one: tc -> stream -> fused -> split).
 int g_apply_path = -1;  // -1: not read from the environment yet
 int apply_path_override() {
   if (g_apply_path < 0) {
     const char* e = getenv("MLORA_APPLY_PATH");
     g_apply_path = e == nullptr ? 0 : strcmp(e, "fused") == 0 ? 1 : strcmp(e, "split") == 0 ? 2
-                 : strcmp(e, "stream") == 0 ? 3 : 0;
+                 : strcmp(e, "stream") == 0 ? 3 : strcmp(e, "tc") == 0 ? 4 : 0;
   }
   return g_apply_path;
 }
@@ -84,7 +84,7 @@ const char* mlora_last_error(void) { return g_err; }
 int mlora_version(void) { return 100; }
 int mlora_last_apply_path(void) { return g_last_apply_path; }
 
-void mlora_set_apply_path(int path) { g_apply_path = (path >= 0 && path <= 3) ? path : 0; }
+void mlora_set_apply_path(int path) { g_apply_path = (path >= 0 && path <= 4) ? path : 0; }
 
 int mlora_get_apply_path(void) { return apply_path_override(); }
 void mlora_set_pdl(int enable) { g_pdl = enable ? 1 : 0; }
@@ -219,7 +219,47 @@ int apply_impl(const void* x, int64_t rows, int64_t in_dim, int64_t x_row_stride
   // one CTA per SM busy whatever the slot count; measured 2x faster than the
   // fused kernel at 512 tokens x 128 adapters), the fused kernel below that
   // (one launch, shorter dependency chain: 2.2x faster at 64 tokens x 32 adapters).
-  const bool stream_pref = forced == 3 || (forced == 0 && rows >= 256 && meta->max_len <= 64);
+  // Long segments (prefill) go to the tensor-core kernels when the shape fits them.
+  const bool tc_pref = forced == 4 || (forced == 0 && meta->max_len >= 64);
+  bool tcable = tc_pref && es == 2 && max_rank == 64 && in_dim % 64 == 0 && x != nullptr && aligned(x, 16) &&
+                x_row_stride % 8 == 0 && mid != nullptr && aligned(mid, 16) && mid_row_stride % 8 == 0 &&
+                mid_row_stride >= (int64_t)n * max_rank && (mids == nullptr || mids[0] == mid) && rows <= INT32_MAX;
+  for (int i = 0; i < n && tcable; ++i)
+    tcable = a_stacks[i] != nullptr && b_stacks[i] != nullptr && ys[i] != nullptr && aligned(a_stacks[i], 16) &&
+             aligned(b_stacks[i], 16) && aligned(ys[i], 16) && y_row_strides[i] % 8 == 0 && out_dims[i] % 8 == 0;
+  if (tcable) {
+    mlora::PrefillLaunch pl{};
+    pl.x = x;
+    pl.x_stride = x_row_stride;
+    pl.n_mod = n;
+    for (int i = 0; i < n; ++i) {
+      pl.mod[i].a = a_stacks[i];
+      pl.mod[i].b = b_stacks[i];
+      pl.mod[i].y = ys[i];
+      pl.mod[i].y_stride = y_row_strides[i];
+      pl.mod[i].out_dim = (int)out_dims[i];
+    }
+    pl.mid = mid;
+    pl.mid_stride = mid_row_stride;
+    pl.seg_indptr = meta->seg_indptr;
+    pl.weight_indices = meta->weight_indices;
+    pl.lora_ranks = meta->lora_ranks;
+    pl.scalings = meta->scalings;
+    pl.scalings_dtype = meta->scalings_dtype;
+    pl.bs = meta->bs;
+    pl.S = (int)rows;
+    pl.in_dim = (int)in_dim;
+    pl.R = (int)max_rank;
+    pl.num_slots = meta->num_slots;
+    pl.status = status;
+    const cudaError_t e = mlora::launch_apply_prefill(pl, dtype, (cudaStream_t)stream, pdl_on());
+    if (e == cudaSuccess) {
+      g_last_apply_path = 4;
+      return MLORA_OK;
+    }
+    if (e != cudaErrorNotSupported) return cuda_status(e, "tensor-core apply_lora launch");
+  }
+  const bool stream_pref = forced == 3 || forced == 4 || (forced == 0 && rows >= 256 && meta->max_len <= 64);
   bool streamable = stream_pref && es == 2 && x != nullptr && aligned(x, 16) &&
                     x_row_stride % 8 == 0 && in_dim % 16 == 0 && max_rank % 8 == 0 && max_rank <= 64 &&
                     mid != nullptr && aligned(mid, 16) && mid_row_stride % 8 == 0 &&
@@ -259,7 +299,7 @@ int apply_impl(const void* x, int64_t rows, int64_t in_dim, int64_t x_row_stride
     }
     if (e != cudaErrorNotSupported) return cuda_status(e, "streaming apply_lora launch");
   }
-  bool fusable = (forced == 0 || forced == 1 || forced == 3) && es == 2 && meta->max_len <= 16 && rows <= 64LL * meta->num_slots && x != nullptr &&
+  bool fusable = forced != 2 && es == 2 && meta->max_len <= 16 && rows <= 64LL * meta->num_slots && x != nullptr &&
                  x_row_stride % 8 == 0 && aligned(x, 16);
   for (int i = 0; i < n && fusable; ++i)
     fusable = a_stacks[i] != nullptr && b_stacks[i] != nullptr && ys[i] != nullptr && aligned(a_stacks[i], 16) &&

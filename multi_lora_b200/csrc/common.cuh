@@ -46,11 +46,13 @@ template <typename T>
 struct Num;
 template <>
 struct Num<__nv_bfloat16> {
+  static constexpr bool is_bf16 = true;
   static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
   static __device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
 };
 template <>
 struct Num<__half> {
+  static constexpr bool is_bf16 = false;
   static __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
   static __device__ __forceinline__ __half from_f(float v) { return __float2half_rn(v); }
 };

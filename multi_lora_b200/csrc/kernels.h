@@ -1,6 +1,7 @@
 // Internal launch interface between the C-ABI layer (capi.cu) and the kernels.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -118,6 +119,53 @@ struct StreamArgs {
   uint32_t* status;
 };
 cudaError_t launch_apply_stream(const StreamArgs& a, int dtype, cudaStream_t st, bool pdl);
+
+// Tensor-core apply for long segments (csrc/prefill_tc.cu).
+constexpr int kMaxPrefillModules = 4;
+struct PrefillModule {
+  const void* a;          // A stack [K, R, in], contiguous
+  const void* b;          // B stack [K, out, R], contiguous
+  void* y;                // [S, out] at y_stride, updated in place
+  int64_t y_stride;
+  int out_dim;
+};
+// What the C ABI hands over; the launcher turns it into tensor maps.
+struct PrefillLaunch {
+  const void* x;
+  int64_t x_stride;
+  PrefillModule mod[kMaxPrefillModules];
+  int n_mod;
+  void* mid;              // [S, >= n_mod * R] at mid_stride: projection m in columns [m*R, m*R + rank)
+  int64_t mid_stride;
+  const int32_t* seg_indptr;
+  const int32_t* weight_indices;
+  const int32_t* lora_ranks;
+  const void* scalings;
+  int scalings_dtype;
+  int bs, S, in_dim, R, num_slots;
+  uint32_t* status;
+};
+// Kernel parameter block (passed as __grid_constant__; tensor maps are 64-byte aligned).
+struct PrefillArgs {
+  CUtensorMap x_map;                          // x [S, in], box 64 x 128
+  CUtensorMap mid_map;                        // mid [S, n_mod * R], box 64 x 128
+  CUtensorMap a_map[kMaxPrefillModules];      // A [K * R, in], box 64 x R
+  CUtensorMap b_map[kMaxPrefillModules];      // B [K * out, R], box 64 x 128
+  CUtensorMap y_map[kMaxPrefillModules];      // y [S, out], box 64 x 128
+  PrefillModule mod[kMaxPrefillModules];
+  int n_mod;
+  void* mid;
+  int64_t mid_stride;
+  const int32_t* seg_indptr;
+  const int32_t* weight_indices;
+  const int32_t* lora_ranks;
+  const void* scalings;
+  int scalings_dtype;
+  int bs, S, in_dim, R, num_slots;
+  int tc_stages;                              // shrink ring depth (set by the launcher)
+  uint32_t* status;
+};
+cudaError_t launch_apply_prefill(const PrefillLaunch& l, int dtype, cudaStream_t st, bool pdl);
 
 // Sets the message mlora_last_error() returns on this thread; returns `code`.
 int report_error(int code, const char* msg);

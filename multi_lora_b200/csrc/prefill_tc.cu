@@ -1,0 +1,450 @@
+// apply_lora for long segments (prefill) on the fifth-generation tensor cores.
+//
+// Semantics are those of LoRABackend.apply_lora (backend/base.py:60-89 of the
+// reference): mid = T(x @ A[slot, :rank].T) with fp32 accumulation
+// (sgemm_lora_a.py:11-115, the GEMM variant), then
+// y = T(T(scaling * mid @ B[slot, :, :rank].T) + y) (sgemm_lora_b.py:11-90),
+// for up to four projections that share x and the routing (q/k/v, gate/up).
+//
+// Each segment's rows are cut into tiles of 128 tokens (the last one ragged;
+// rows past the segment are computed but never stored).
+//   lora_shrink_tc_kernel: one CTA per tile. TMA streams 64-column blocks of x
+//     (128 x 64) and of every projection's A[slot] (R x 64, R = 64) through a
+//     3-4 stage ring in the 128-byte-swizzled K-major layout; one thread issues
+//     tcgen05.mma (M = 128, N = n_proj * 64, K = 16) into a TMEM accumulator;
+//     every stage is released by tcgen05.commit. The epilogue reads TMEM row
+//     by row (thread = token), rounds to T once and writes mid columns < rank.
+//   lora_expand_tc_kernel: one CTA per (tile, projection, 128-column block of
+//     out). TMA brings the mid tile, B[slot, block, :] and the y tile; four
+//     tcgen05.mma (K = 64) fill a 128 x 128 TMEM accumulator; the epilogue
+//     fuses the scaling, the rounding and the residual add and stores the
+//     segment's rows with 16-byte stores.
+// Shapes: bf16/f16, max_rank 64, in % 64 == 0, out % 8 == 0. Adapter weights
+// are requested before griddepcontrol.wait; x, mid and y after it. Waits are
+// bounded; TMEM is always freed.
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "tc.cuh"
+
+namespace mlora {
+
+constexpr int kTcThreads = 128;
+constexpr int kTcTileM = 128;  // tokens per tile
+constexpr int kTcBK = 64;      // K block (one 128-byte swizzle row)
+constexpr int kTcBN = 128;     // expand output columns per CTA
+constexpr int kTcR = 64;       // max_rank handled by these kernels
+
+struct TcTile {
+  int seg, row0, rows, slot, rank;
+};
+
+// Warp 0: tile index -> segment, first row, valid rows, slot and rank. Segments
+// with rank 0, an out-of-range slot or bad bounds contribute no tiles. Returns
+// false (for every lane) past the last tile.
+__device__ bool tc_find_tile(const PrefillArgs& p, int tile, TcTile& out) {
+  const int lane = threadIdx.x & 31;
+  const bool reporter = blockIdx.x == 0 && blockIdx.y == 0;
+  int base = 0;
+  for (int s0 = 0; s0 < p.bs; s0 += 32) {
+    const int seg = s0 + lane;
+    int st = 0, en = 0, slot = -1, rank = 0;
+    if (seg < p.bs) {
+      slot = __ldg(p.weight_indices + seg);
+      st = __ldg(p.seg_indptr + seg);
+      en = __ldg(p.seg_indptr + seg + 1);
+      if (slot < 0 || slot >= p.num_slots) {
+        if (reporter) flag_error(p.status, kErrSlotRange);
+        slot = -1;
+      } else if (st < 0 || en < st || en > p.S) {
+        if (reporter) flag_error(p.status, kErrIndptr);
+        slot = -1;
+      } else {
+        rank = __ldg(p.lora_ranks + slot);
+        if (rank < 0 || rank > p.R) {
+          if (reporter) flag_error(p.status, kErrRankRange);
+          rank = rank < 0 ? 0 : p.R;
+        }
+      }
+    }
+    const int n = (slot >= 0 && rank > 0) ? (en - st + kTcTileM - 1) / kTcTileM : 0;
+    int incl = n;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    const bool mine = tile >= base + incl - n && tile < base + incl;
+    const unsigned hit = __ballot_sync(0xffffffffu, mine);
+    if (hit != 0u) {
+      const int src = __ffs(hit) - 1;
+      const int k = tile - (base + __shfl_sync(0xffffffffu, incl - n, src));
+      out.seg = s0 + src;
+      const int s_st = __shfl_sync(0xffffffffu, st, src), s_en = __shfl_sync(0xffffffffu, en, src);
+      out.row0 = s_st + k * kTcTileM;
+      out.rows = min(kTcTileM, s_en - out.row0);
+      out.slot = __shfl_sync(0xffffffffu, slot, src);
+      out.rank = __shfl_sync(0xffffffffu, rank, src);
+      return true;
+    }
+    base += __shfl_sync(0xffffffffu, incl, 31);
+  }
+  return false;
+}
+
+__device__ __forceinline__ const CUtensorMap* tc_map(const CUtensorMap* maps, int m) { return maps + m; }
+
+// ---------------------------------------------------------------------------
+// shrink: mid[tile rows, m*R : m*R + rank] for every projection m
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(kTcThreads) lora_shrink_tc_kernel(const __grid_constant__ PrefillArgs p) {
+  constexpr uint32_t X_BYTES = kTcTileM * kTcBK * 2;  // 16 KB
+  constexpr uint32_t A_BYTES = kTcR * kTcBK * 2;      // 8 KB per projection
+  extern __shared__ __align__(1024) unsigned char s_raw[];
+  __shared__ __align__(8) uint64_t full[4], empty[4], done;
+  __shared__ uint32_t s_tmem;
+  __shared__ TcTile s_tile;
+  __shared__ int s_ok;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(s_raw) + 1023) & ~uintptr_t(1023));
+  if (warp == 0) {
+    TcTile t;
+    const bool ok = tc_find_tile(p, blockIdx.x, t);
+    if (lane == 0) {
+      s_ok = ok;
+      if (ok) s_tile = t;
+    }
+  }
+  __syncthreads();
+  if (!s_ok) {
+    pdl_trigger();
+    return;
+  }
+  const TcTile t = s_tile;
+  const int nm = p.n_mod;
+  const int ns = p.tc_stages;
+  const uint32_t stage_bytes = X_BYTES + (uint32_t)nm * A_BYTES;
+  const uint32_t ncols = nm == 1 ? 64u : nm == 2 ? 128u : 256u;
+  if (tid == 0) {
+    for (int s = 0; s < ns; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(&s_tmem, ncols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  pdl_trigger();
+  const uint32_t taddr = s_tmem;
+  const int KB = p.in_dim / kTcBK;
+  bool ok = true;
+
+  if (tid == 0) {  // ---- TMA producer ----
+    auto issue_a = [&](int kb) {
+      const int s = kb % ns;
+      unsigned char* st = smem + (size_t)s * stage_bytes;
+      mbar_arrive_expect_tx(&full[s], stage_bytes);
+      for (int m = 0; m < nm; ++m)
+        tma_load_2d(st + X_BYTES + m * A_BYTES, tc_map(p.a_map, m), kb * kTcBK, t.slot * p.R, &full[s]);
+    };
+    auto issue_x = [&](int kb) {
+      unsigned char* st = smem + (size_t)(kb % ns) * stage_bytes;
+      tma_load_2d(st, &p.x_map, kb * kTcBK, t.row0, &full[kb % ns]);
+    };
+    const int pre = min(ns, KB);
+    for (int kb = 0; kb < pre; ++kb) issue_a(kb);  // adapter weights: before the wait
+    pdl_wait();                                     // x comes from earlier kernels
+    for (int kb = 0; kb < pre; ++kb) issue_x(kb);
+    for (int kb = pre; kb < KB && ok; ++kb) {
+      ok = mbar_wait(&empty[kb % ns], ((kb / ns) - 1) & 1, p.status);
+      if (ok) {
+        issue_a(kb);
+        issue_x(kb);
+      }
+    }
+  } else if (tid == 32) {  // ---- MMA issuer ----
+    const uint32_t idesc = umma_idesc_f16(Num<T>::is_bf16, kTcTileM, nm * kTcR);
+    for (int kb = 0; kb < KB && ok; ++kb) {
+      const int s = kb % ns;
+      ok = mbar_wait(&full[s], (kb / ns) & 1, p.status);
+      if (!ok) break;
+      tc_fence_after();
+      unsigned char* st = smem + (size_t)s * stage_bytes;
+      const uint64_t ad = umma_desc_sw128(st), bd = umma_desc_sw128(st + X_BYTES);
+#pragma unroll
+      for (int k = 0; k < kTcBK / 16; ++k) umma_f16(taddr, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+      umma_commit(&empty[s]);
+    }
+    umma_commit(&done);
+  }
+  __syncwarp();
+  const bool fin = mbar_wait(&done, 0, p.status);
+  tc_fence_after();
+
+  // ---- epilogue: thread = token row; round once to T; columns < rank only ----
+  const int r = warp * 32 + lane;
+  const bool row_ok = fin && r < t.rows;
+  T* mid = static_cast<T*>(p.mid) + (int64_t)(t.row0 + r) * p.mid_stride;
+  for (int m = 0; m < nm; ++m) {
+    for (int h = 0; h < kTcR / 32; ++h) {
+      float v[32];
+      tmem_ld32(taddr + ((uint32_t)(warp * 32) << 16) + (uint32_t)(m * kTcR + h * 32), v);
+      if (row_ok) {
+        T* dst = mid + m * p.R + h * 32;
+        if (t.rank >= h * 32 + 32) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 u;
+            u.x = Pack2<T>::pack(Num<T>::from_f(v[8 * q + 0]), Num<T>::from_f(v[8 * q + 1]));
+            u.y = Pack2<T>::pack(Num<T>::from_f(v[8 * q + 2]), Num<T>::from_f(v[8 * q + 3]));
+            u.z = Pack2<T>::pack(Num<T>::from_f(v[8 * q + 4]), Num<T>::from_f(v[8 * q + 5]));
+            u.w = Pack2<T>::pack(Num<T>::from_f(v[8 * q + 6]), Num<T>::from_f(v[8 * q + 7]));
+            *reinterpret_cast<uint4*>(dst + 8 * q) = u;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (h * 32 + i < t.rank) dst[i] = Num<T>::from_f(v[i]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_free(taddr, ncols);
+}
+
+// ---------------------------------------------------------------------------
+// expand: y[tile rows, block] = T(T(scale * mid @ B^T) + y)
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(kTcThreads) lora_expand_tc_kernel(const __grid_constant__ PrefillArgs p) {
+  constexpr uint32_t M_BYTES = kTcTileM * kTcR * 2;   // mid tile 16 KB
+  constexpr uint32_t B_BYTES = kTcBN * kTcR * 2;      // 16 KB
+  constexpr uint32_t Y_BYTES = kTcTileM * kTcBK * 2;  // one 64-column y box, 16 KB
+  extern __shared__ __align__(1024) unsigned char s_raw[];
+  __shared__ __align__(8) uint64_t bar_load, bar_mma;
+  __shared__ uint32_t s_tmem;
+  __shared__ TcTile s_tile;
+  __shared__ int s_ok;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(s_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* s_mid = smem;
+  unsigned char* s_b = smem + M_BYTES;
+  unsigned char* s_y = smem + M_BYTES + B_BYTES;
+  // blockIdx.x -> (projection, 128-column block)
+  int m = 0, blk = blockIdx.x;
+  while (m + 1 < p.n_mod && blk >= (p.mod[m].out_dim + kTcBN - 1) / kTcBN) {
+    blk -= (p.mod[m].out_dim + kTcBN - 1) / kTcBN;
+    ++m;
+  }
+  const PrefillModule& mod = p.mod[m];
+  const int n0 = blk * kTcBN;
+  if (warp == 0) {
+    TcTile t;
+    const bool ok = tc_find_tile(p, blockIdx.y, t);
+    if (lane == 0) {
+      s_ok = ok && n0 < mod.out_dim;
+      if (ok) s_tile = t;
+    }
+  }
+  __syncthreads();
+  if (!s_ok) {
+    pdl_trigger();
+    return;
+  }
+  const TcTile t = s_tile;
+  if (tid == 0) {
+    mbar_init(&bar_load, 1);
+    mbar_init(&bar_mma, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(&s_tmem, kTcBN);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  pdl_trigger();
+  const uint32_t taddr = s_tmem;
+
+  if (tid == 0) {
+    mbar_arrive_expect_tx(&bar_load, M_BYTES + B_BYTES + 2 * Y_BYTES);
+    tma_load_2d(s_b, tc_map(p.b_map, m), 0, t.slot * mod.out_dim + n0, &bar_load);  // weights: before the wait
+    pdl_wait();  // mid (shrink kernel) and y (base projection)
+    tma_load_2d(s_mid, &p.mid_map, m * p.R, t.row0, &bar_load);
+    tma_load_2d(s_y, tc_map(p.y_map, m), n0, t.row0, &bar_load);
+    tma_load_2d(s_y + Y_BYTES, tc_map(p.y_map, m), n0 + kTcBK, t.row0, &bar_load);
+  }
+  bool ok = mbar_wait(&bar_load, 0, p.status);
+  if (t.rank < kTcR) {  // columns >= rank of mid (stale) and of B (stale) contribute zero
+    const int w = kTcR - t.rank;
+    for (int e = tid; e < kTcTileM * w; e += kTcThreads) {
+      const int row = e / w, col = t.rank + e % w;
+      *reinterpret_cast<T*>(s_mid + sw128_offset(row, col)) = Num<T>::from_f(0.f);
+      *reinterpret_cast<T*>(s_b + sw128_offset(row, col)) = Num<T>::from_f(0.f);  // kTcBN == kTcTileM rows
+    }
+    fence_proxy_async_smem();
+  }
+  __syncthreads();
+  if (tid == 0 && ok) {
+    tc_fence_after();
+    const uint32_t idesc = umma_idesc_f16(Num<T>::is_bf16, kTcTileM, kTcBN);
+    const uint64_t ad = umma_desc_sw128(s_mid), bd = umma_desc_sw128(s_b);
+#pragma unroll
+    for (int k = 0; k < kTcR / 16; ++k) umma_f16(taddr, ad + 2 * k, bd + 2 * k, idesc, k != 0);
+    umma_commit(&bar_mma);
+  }
+  __syncwarp();
+  ok = __syncthreads_and(ok) && mbar_wait(&bar_mma, 0, p.status);
+  tc_fence_after();
+
+  // ---- epilogue: thread = token row ----
+  const int r = warp * 32 + lane;
+  const bool row_ok = ok && r < t.rows;
+  float scale;
+  switch (p.scalings_dtype) {
+    case kBF16: scale = __bfloat162float(__ldg(static_cast<const __nv_bfloat16*>(p.scalings) + t.slot)); break;
+    case kF16: scale = __half2float(__ldg(static_cast<const __half*>(p.scalings) + t.slot)); break;
+    default: scale = __ldg(static_cast<const float*>(p.scalings) + t.slot); break;
+  }
+  T* yrow = static_cast<T*>(mod.y) + (int64_t)(t.row0 + r) * mod.y_stride + n0;
+#pragma unroll 1
+  for (int c = 0; c < kTcBN / 32; ++c) {
+    float v[32];
+    tmem_ld32(taddr + ((uint32_t)(warp * 32) << 16) + (uint32_t)(c * 32), v);
+    if (row_ok) {
+      const unsigned char* yb = s_y + (c >> 1) * Y_BYTES;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int col = (c & 1) * 32 + q * 8;  // column within the 64-column box
+        if (n0 + c * 32 + q * 8 < mod.out_dim) {
+          const uint4 yin = *reinterpret_cast<const uint4*>(yb + sw128_offset(r, col));
+          const uint32_t in[4] = {yin.x, yin.y, yin.z, yin.w};
+          uint32_t o[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            o[i] = Pack2<T>::pack(Num<T>::from_f(round_to<T>(v[8 * q + 2 * i] * scale) + Pack2<T>::lo(in[i])),
+                                  Num<T>::from_f(round_to<T>(v[8 * q + 2 * i + 1] * scale) + Pack2<T>::hi(in[i])));
+          *reinterpret_cast<uint4*>(yrow + c * 32 + q * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_free(taddr, kTcBN);
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+namespace {
+
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encoder() {
+  static EncodeTiled fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      (void)cudaGetLastError();
+      return (EncodeTiled) nullptr;
+    }
+    return reinterpret_cast<EncodeTiled>(f);
+  }();
+  return fn;
+}
+
+// 2-D map over a row-major [outer, inner] matrix with rows `stride_elems` apart;
+// box {64, box_rows}, 128-byte swizzle, zero fill out of bounds.
+bool encode_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, uint64_t outer, uint64_t stride_elems,
+               uint32_t box_rows) {
+  EncodeTiled enc = encoder();
+  if (enc == nullptr) return false;
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {stride_elems * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kTcBK, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(map, dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+             const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename K>
+bool ensure_smem_tc(K kern, int bytes) {
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  return true;
+}
+
+template <typename T>
+cudaError_t launch_prefill_t(PrefillArgs& a, int dtype, cudaStream_t st, bool pdl) {
+  const int nm = a.n_mod;
+  a.tc_stages = nm <= 2 ? 4 : 3;
+  const int shrink_smem = a.tc_stages * (kTcTileM * kTcBK * 2 + nm * kTcR * kTcBK * 2) + 1024;
+  const int expand_smem = (kTcTileM * kTcR * 2) + (kTcBN * kTcR * 2) + 2 * (kTcTileM * kTcBK * 2) + 1024;
+  auto ks = lora_shrink_tc_kernel<T>;
+  auto ke = lora_expand_tc_kernel<T>;
+  // largest shrink configuration: 3 stages of x + four projections' A blocks (4 stages of two are smaller)
+  static const bool smem_ok = ensure_smem_tc(ks, 3 * (kTcTileM * kTcBK * 2 + 4 * kTcR * kTcBK * 2) + 1024) &&
+                              ensure_smem_tc(ke, expand_smem);
+  if (!smem_ok) return cudaErrorNotSupported;
+  const long long tiles = (a.S + kTcTileM - 1) / kTcTileM + (long long)a.bs;
+  if (tiles > 65535) return cudaErrorNotSupported;
+  int blocks = 0;
+  for (int m = 0; m < nm; ++m) blocks += (a.mod[m].out_dim + kTcBN - 1) / kTcBN;
+  cudaError_t e = launch_kernel(ks, dim3((unsigned)tiles), dim3(kTcThreads), shrink_smem, st, pdl, a);
+  if (e != cudaSuccess) return e;
+  return launch_kernel(ke, dim3((unsigned)blocks, (unsigned)tiles), dim3(kTcThreads), expand_smem, st, true, a);
+}
+
+}  // namespace
+
+cudaError_t launch_apply_prefill(const PrefillLaunch& l, int dtype, cudaStream_t st, bool pdl) {
+  if (dtype != kBF16 && dtype != kF16) return cudaErrorNotSupported;
+  if (l.n_mod < 1 || l.n_mod > kMaxPrefillModules || l.R != kTcR || l.in_dim % kTcBK != 0) return cudaErrorNotSupported;
+  PrefillArgs a{};
+  a.n_mod = l.n_mod;
+  a.mid = l.mid;
+  a.mid_stride = l.mid_stride;
+  a.seg_indptr = l.seg_indptr;
+  a.weight_indices = l.weight_indices;
+  a.lora_ranks = l.lora_ranks;
+  a.scalings = l.scalings;
+  a.scalings_dtype = l.scalings_dtype;
+  a.bs = l.bs;
+  a.S = l.S;
+  a.in_dim = l.in_dim;
+  a.R = l.R;
+  a.num_slots = l.num_slots;
+  a.status = l.status;
+  bool ok = encode_2d(&a.x_map, l.x, dtype, (uint64_t)l.in_dim, (uint64_t)l.S, (uint64_t)l.x_stride, kTcTileM) &&
+            encode_2d(&a.mid_map, l.mid, dtype, (uint64_t)l.n_mod * l.R, (uint64_t)l.S, (uint64_t)l.mid_stride, kTcTileM);
+  for (int m = 0; m < l.n_mod && ok; ++m) {
+    a.mod[m] = l.mod[m];
+    ok = encode_2d(&a.a_map[m], l.mod[m].a, dtype, (uint64_t)l.in_dim, (uint64_t)l.num_slots * l.R, (uint64_t)l.in_dim,
+                   kTcR) &&
+         encode_2d(&a.b_map[m], l.mod[m].b, dtype, (uint64_t)l.R, (uint64_t)l.num_slots * l.mod[m].out_dim,
+                   (uint64_t)l.R, kTcBN) &&
+         encode_2d(&a.y_map[m], l.mod[m].y, dtype, (uint64_t)l.mod[m].out_dim, (uint64_t)l.S,
+                   (uint64_t)l.mod[m].y_stride, kTcTileM);
+  }
+  if (!ok) return cudaErrorNotSupported;
+  return dtype == kBF16 ? launch_prefill_t<__nv_bfloat16>(a, dtype, st, pdl) : launch_prefill_t<__half>(a, dtype, st, pdl);
+}
+
+}  // namespace mlora

@@ -1,0 +1,112 @@
+// sm_100a fifth-generation tensor core (tcgen05) and tensor-map TMA helpers.
+//
+// Operand tiles live in shared memory in the K-major, 128-byte-swizzled
+// layout that a TMA tensor load with CU_TENSOR_MAP_SWIZZLE_128B writes: rows of
+// 64 bf16/f16 (128 B), the 16-byte chunk index XOR-ed with (row % 8), tiles
+// aligned to 1024 B. Accumulators live in tensor memory (TMEM), allocated per
+// CTA and read back row-per-thread with tcgen05.ld.
+#pragma once
+
+#include <cuda.h>
+#include <stdint.h>
+
+#include "tma.cuh"
+
+namespace mlora {
+
+// ---- tensor-map TMA (no multicast) -------------------------------------------
+
+// 2-D tiled load of box {c0.., c1..} (inner, outer coordinates in elements)
+// into shared memory; completes its bytes on `bar`. c0 * element size must be a
+// multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ---- UMMA descriptors ---------------------------------------------------------
+
+// Shared-memory matrix descriptor: K-major, SWIZZLE_128B, 8-row groups 1024 B
+// apart (rows of 128 B packed). Advance by 32 B (one K=16 step) with `+ 2`.
+__device__ __forceinline__ uint64_t umma_desc_sw128(const void* tile) {
+  const uint64_t a = (uint64_t)((smem_addr(tile) >> 4) & 0x3FFFu);
+  return a | (1ull << 16)      // leading byte offset (unused for swizzled K-major)
+         | (64ull << 32)       // stride byte offset: 1024 B between 8-row groups
+         | (1ull << 46)        // descriptor version (sm_100)
+         | (2ull << 61);       // layout: SWIZZLE_128B
+}
+
+// Instruction descriptor of tcgen05.mma.kind::f16: fp32 accumulate, A and B of
+// the same 16-bit type (bf16 when `bf16`), both K-major, shape M x N.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(bool bf16, int M, int N) {
+  return (1u << 4)                                   // D: f32
+         | ((bf16 ? 1u : 0u) << 7)                   // A type
+         | ((bf16 ? 1u : 0u) << 10)                  // B type
+         | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// ---- tcgen05 ------------------------------------------------------------------
+
+// D[tmem] (+)= A[smem] * B[smem]^T, issued by one thread.
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive (once) on `bar` when every tcgen05.mma this thread issued so far has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Whole warp: allocate `ncols` TMEM columns (power of two >= 32); the base
+// address is written to shared memory at `dst`.
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+// Whole warp: free an allocation.
+__device__ __forceinline__ void tmem_free(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Whole warp: 32 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Byte offset of element (row, col) in a 128-byte-swizzled tile of 64-column rows.
+__device__ __forceinline__ uint32_t sw128_offset(int row, int col) {
+  return (uint32_t)row * 128u + ((uint32_t)(((col >> 3) ^ (row & 7)) << 4)) + (uint32_t)(col & 7) * 2u;
+}
+
+}  // namespace mlora

@@ -242,6 +242,69 @@ def test_fused_apply_many_segments_and_cluster16(cuda_dev):
     _check_apply(c, cuda_dev, torch.bfloat16, expect_path=1, force="fused")
 
 
+TC_SHAPES = [
+    # n_in, n_out, R, ranks, lens
+    (512, 384, 64, [64, 64, 64], [300, 129, 64]),              # ragged tiles (300 = 128 + 128 + 44), 1-row tile
+    (1024, 1000, 64, [64, 8, 33, 0], [200, 150, 77, 90]),      # ranks < R (NaN-planted tails), base segment,
+                                                               # out % 128 != 0 (partial column block)
+    (4096, 1024, 64, [64] * 8, [469, 845, 454, 989, 348, 314, 495, 426]),  # cfg3 k/v projection, full size
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", TC_SHAPES, ids=lambda s: f"{s[0]}x{s[1]}r{s[2]}s{sum(s[4])}")
+def test_tc_apply_matches_oracle(cuda_dev, dtype, shape):
+    """tcgen05 shrink/expand pair (the automatic choice for segments of >= 64 rows)."""
+    n_in, n_out, R, ranks, lens = shape
+    c = _case(hash((n_in, n_out, R, 5)) % 1000, dtype, n_in, n_out, R, ranks, lens, cuda_dev)
+    _check_apply(c, cuda_dev, dtype, expect_path=4)
+
+
+def test_tc_group_matches_separate_projections(cuda_dev):
+    """q/k/v-like group on the tensor-core pair: mid [S, 3R] holds one column block per projection."""
+    import ctypes
+
+    dev, dt = cuda_dev, torch.bfloat16
+    g = torch.Generator().manual_seed(77)
+    outs, R, ranks, lens, n_in = (512, 256, 128), 64, [64, 8, 33], [150, 90, 70], 640
+    K, S = len(ranks), sum(lens)
+    widx = [0, 1, 2]
+    scal = [0.5 + i for i in range(K)]
+    x = torch.randn(S, n_in, generator=g).to(dt)
+    meta = C.make_meta(lens, widx, ranks, scal, dev)
+    As, Bs, ys, y0 = [], [], [], []
+    for o in outs:
+        a = (torch.randn(K, R, n_in, generator=g) * n_in ** -0.5).to(dt)
+        b = (torch.randn(K, o, R, generator=g) * 0.05).to(dt)
+        for s_, r in enumerate(ranks):
+            a[s_, r:] = float("nan")
+            b[s_, :, r:] = float("nan")
+        yb = torch.randn(S, o, generator=g).to(dt)
+        As.append(a.to(dev))
+        Bs.append(b.to(dev))
+        y0.append(yb)
+        ys.append(yb.to(dev).clone())
+    xd = x.to(dev)
+    mid = torch.zeros(S, 3 * R, dtype=dt, device=dev)
+    n = len(outs)
+    P = ctypes.c_void_p
+    arr = lambda vals, t: (t * n)(*vals)  # noqa: E731
+    m = meta.struct()
+    rc = _native.capi().mlora_apply_lora_group(
+        xd.data_ptr(), S, n_in, n_in, n, arr([a.data_ptr() for a in As], P), arr([b.data_ptr() for b in Bs], P),
+        arr(list(outs), ctypes.c_int64), arr([y.data_ptr() for y in ys], P),
+        arr([y.stride(0) for y in ys], ctypes.c_int64), R, ctypes.byref(m), mid.data_ptr(), 3 * R, 0, None,
+        torch.cuda.current_stream().cuda_stream)
+    C.check(rc)
+    assert _native.capi().mlora_last_apply_path() == 4
+    torch.cuda.synchronize()
+    ind = meta.seg_indptr.cpu().numpy()
+    for a, b, yb, y in zip(As, Bs, y0, ys):
+        want = O.apply_lora_fp32(C.f32(x), np.nan_to_num(C.f32(a)), np.nan_to_num(C.f32(b)), ind, widx, ranks, scal,
+                                 len(lens), C.f32(yb))
+        np.testing.assert_allclose(C.f32(y), want, rtol=RTOL, atol=ATOL)
+
+
 def test_stream_apply_many_slots_and_long_segments(cuda_dev):
     """cfg5-like routing (128 slots, 512 one-token segments), one slot with 100
     tokens (13 tiles), and more segments than one slot's tile."""
