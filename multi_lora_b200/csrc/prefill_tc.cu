@@ -8,12 +8,16 @@
 //
 // Each segment's rows are cut into tiles of 128 tokens (the last one ragged;
 // rows past the segment are computed but never stored).
-//   lora_shrink_tc_kernel: one CTA per tile. TMA streams 64-column blocks of x
+//   lora_shrink_tc_kernel: one CTA per (tile, K split). TMA streams 64-column blocks of x
 //     (128 x 64) and of every projection's A[slot] (R x 64, R = 64) through a
 //     3-4 stage ring in the 128-byte-swizzled K-major layout; one thread issues
 //     tcgen05.mma (M = 128, N = n_proj * 64, K = 16) into a TMEM accumulator;
 //     every stage is released by tcgen05.commit. The epilogue reads TMEM row
 //     by row (thread = token), rounds to T once and writes mid columns < rank.
+//     When there are few tiles the input dim is split over a thread-block
+//     cluster (up to 8 CTAs): each CTA parks its fp32 partial tile in its own
+//     shared memory and every CTA sums the partials of its share of the rows
+//     over distributed shared memory, in split order (deterministic).
 //   lora_expand_tc_kernel: one CTA per (tile, projection, 128-column block of
 //     out). TMA brings the mid tile, B[slot, block, :] and the y tile; four
 //     tcgen05.mma (K = 64) fill a 128 x 128 TMEM accumulator; the epilogue
@@ -110,21 +114,23 @@ __global__ void __launch_bounds__(kTcThreads) lora_shrink_tc_kernel(const __grid
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(s_raw) + 1023) & ~uintptr_t(1023));
+  // blockIdx.y = tile, blockIdx.x = K split (one thread-block cluster per tile when splits > 1)
   if (warp == 0) {
     TcTile t;
-    const bool ok = tc_find_tile(p, blockIdx.x, t);
+    const bool ok = tc_find_tile(p, blockIdx.y, t);
     if (lane == 0) {
       s_ok = ok;
       if (ok) s_tile = t;
     }
   }
   __syncthreads();
-  if (!s_ok) {
+  if (!s_ok) {  // uniform over the cluster (same tile)
     pdl_trigger();
     return;
   }
   const TcTile t = s_tile;
   const int nm = p.n_mod;
+  const int splits = gridDim.x, split = blockIdx.x;
   const int ns = p.tc_stages;
   const uint32_t stage_bytes = X_BYTES + (uint32_t)nm * A_BYTES;
   const uint32_t ncols = nm == 1 ? 64u : nm == 2 ? 128u : 256u;
@@ -142,7 +148,9 @@ __global__ void __launch_bounds__(kTcThreads) lora_shrink_tc_kernel(const __grid
   tc_fence_after();
   pdl_trigger();
   const uint32_t taddr = s_tmem;
-  const int KB = p.in_dim / kTcBK;
+  const int KB_all = p.in_dim / kTcBK;
+  const int kb0 = split * KB_all / splits;  // this CTA's K blocks [kb0, kb0 + KB)
+  const int KB = (split + 1) * KB_all / splits - kb0;
   bool ok = true;
 
   if (tid == 0) {  // ---- TMA producer ----
@@ -151,11 +159,11 @@ __global__ void __launch_bounds__(kTcThreads) lora_shrink_tc_kernel(const __grid
       unsigned char* st = smem + (size_t)s * stage_bytes;
       mbar_arrive_expect_tx(&full[s], stage_bytes);
       for (int m = 0; m < nm; ++m)
-        tma_load_2d(st + X_BYTES + m * A_BYTES, tc_map(p.a_map, m), kb * kTcBK, t.slot * p.R, &full[s]);
+        tma_load_2d(st + X_BYTES + m * A_BYTES, tc_map(p.a_map, m), (kb0 + kb) * kTcBK, t.slot * p.R, &full[s]);
     };
     auto issue_x = [&](int kb) {
       unsigned char* st = smem + (size_t)(kb % ns) * stage_bytes;
-      tma_load_2d(st, &p.x_map, kb * kTcBK, t.row0, &full[kb % ns]);
+      tma_load_2d(st, &p.x_map, (kb0 + kb) * kTcBK, t.row0, &full[kb % ns]);
     };
     const int pre = min(ns, KB);
     for (int kb = 0; kb < pre; ++kb) issue_a(kb);  // adapter weights: before the wait
@@ -187,8 +195,56 @@ __global__ void __launch_bounds__(kTcThreads) lora_shrink_tc_kernel(const __grid
   const bool fin = mbar_wait(&done, 0, p.status);
   tc_fence_after();
 
-  // ---- epilogue: thread = token row; round once to T; columns < rank only ----
   const int r = warp * 32 + lane;
+  if (splits > 1) {
+    // ---- split K: fp32 partials into this CTA's shared memory (the ring is
+    // idle now), then each CTA of the cluster sums the splits, in split order,
+    // for its share of the rows and writes them ----
+    const int N = nm * kTcR, PS = N + 4;  // padded row (conflict-free 16-byte stores)
+    float* part = reinterpret_cast<float*>(smem);
+    for (int c = 0; c < N / 32; ++c) {
+      float v[32];
+      tmem_ld32(taddr + ((uint32_t)(warp * 32) << 16) + (uint32_t)(c * 32), v);
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        *reinterpret_cast<float4*>(part + r * PS + c * 32 + 4 * q) =
+            make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    }
+    tc_fence_before();
+    cluster_arrive_release();
+    cluster_wait_acquire();  // every split's partials are in place
+    const int rows_per = (kTcTileM + splits - 1) / splits;
+    const int ra = split * rows_per, rb = min(kTcTileM, ra + rows_per);
+    const uint32_t base = smem_addr(part);
+    const int groups = N / 4;
+    for (int e = tid; e < (rb - ra) * groups; e += kTcThreads) {
+      const int row = ra + e / groups, c4 = (e % groups) * 4;
+      const uint32_t off = (uint32_t)(row * PS + c4) * 4u;
+      float4 acc = ld_dsmem_v4(cluster_map(base + off, 0));
+      for (int q = 1; q < splits; ++q) {
+        const float4 v = ld_dsmem_v4(cluster_map(base + off, (uint32_t)q));
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      if (fin && row < t.rows) {
+        const int m = c4 / kTcR, k = c4 % kTcR;
+        T* dst = static_cast<T*>(p.mid) + (int64_t)(t.row0 + row) * p.mid_stride + m * p.R + k;
+        const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (k + i < t.rank) dst[i] = Num<T>::from_f(a4[i]);
+      }
+    }
+    cluster_arrive_release();
+    cluster_wait_acquire();  // peers are done reading this CTA's partials
+    __syncthreads();
+    if (warp == 1) tmem_free(taddr, ncols);
+    return;
+  }
+
+  // ---- epilogue: thread = token row; round once to T; columns < rank only ----
   const bool row_ok = fin && r < t.rows;
   T* mid = static_cast<T*>(p.mid) + (int64_t)(t.row0 + r) * p.mid_stride;
   for (int m = 0; m < nm; ++m) {
@@ -380,6 +436,18 @@ bool encode_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, ui
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+long long tc_sm_count() {
+  static const int n = [] {
+    int dev = 0, c = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return 148;
+    }
+    return c;
+  }();
+  return n;
+}
+
 template <typename K>
 bool ensure_smem_tc(K kern, int bytes) {
   static std::mutex mu;
@@ -407,7 +475,25 @@ cudaError_t launch_prefill_t(PrefillArgs& a, int dtype, cudaStream_t st, bool pd
   if (tiles > 65535) return cudaErrorNotSupported;
   int blocks = 0;
   for (int m = 0; m < nm; ++m) blocks += (a.mod[m].out_dim + kTcBN - 1) / kTcBN;
-  cudaError_t e = launch_kernel(ks, dim3((unsigned)tiles), dim3(kTcThreads), shrink_smem, st, pdl, a);
+  // K splits: enough shrink CTAs for one per SM (one fits per SM), at least 4 K blocks each, a cluster of <= 8
+  int splits = (int)(tc_sm_count() / tiles);
+  splits = splits < 1 ? 1 : splits > 8 ? 8 : splits;
+  while (splits > 1 && a.in_dim / kTcBK < 4 * splits) --splits;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)splits, (unsigned)tiles);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = shrink_smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = splits;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, ks, a);
   if (e != cudaSuccess) return e;
   return launch_kernel(ke, dim3((unsigned)blocks, (unsigned)tiles), dim3(kTcThreads), expand_smem, st, true, a);
 }

@@ -122,6 +122,16 @@ __device__ __forceinline__ void st_async_v4(uint32_t remote_addr, float a, float
       : "memory");
 }
 
+// 16-byte load from another CTA's shared memory (cluster address from cluster_map).
+__device__ __forceinline__ float4 ld_dsmem_v4(uint32_t cluster_addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(cluster_addr)
+               : "memory");
+  return v;
+}
+
 // Split cluster barrier: arrive (release) early, wait (acquire) late.
 __device__ __forceinline__ void cluster_arrive_release() {
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
