@@ -377,11 +377,17 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg2")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="override the workload's layer count (small cases for profiler captures only; "
+                         "the reported numbers are then not the workload's)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ungrouped", action="store_true",
                     help="one apply_lora call per projection instead of grouping q/k/v and gate/up")
     args = ap.parse_args()
     wl = WORKLOADS[args.workload]
+    if args.layers > 0:
+        wl.layers = args.layers
+        wl.desc += f" [layers overridden to {args.layers}: profiling case]"
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
