@@ -76,6 +76,11 @@ WORKLOADS = {
     "cfg3": Workload("cfg3", "Llama-3-8B-shaped prefill: 32 layers x 7 LoRA projections + 2 RMSNorm, 8 requests of "
                              "128..1024 tokens (seed 0: 4340 tokens), one adapter each, 8 adapters r64 (alpha 128), "
                              "bf16", 4096, 1024, 14336, 32, 4340, 8, 64, 128, requests=8),
+    "cfg4": Workload("cfg4", "Heavy-tail decode with eviction: Llama-2-7B shapes, 32 layers, 256 adapters of rank "
+                             "{8,16,32,64} (alpha 2r), 64-slot pool (max_rank 64, LRU), 256 tokens/step with Zipf(1.1) "
+                             "adapter ids, admission: tokens in draw order until 64 distinct adapters, the rest "
+                             "deferred to the next step; pinned-host slot loads; RMSNorm on; bf16",
+                     4096, 4096, 11008, 32, 256, 256, 64, 128),
     "cfg5": Workload("cfg5", "Llama-3-70B-shaped decode: 80 layers x 7 LoRA projections + 2 RMSNorm, 512 tokens, "
                              "128 adapters r16 (alpha 32), bf16", 8192, 1024, 28672, 80, 512, 128, 16, 32),
 }
@@ -362,6 +367,179 @@ class CpuReference:
                 "per_layer_ms": round(per_layer * 1e3, 3)}
 
 
+POOL_SLOTS = 64
+ZIPF_S = 1.1
+CFG4_RANKS = (8, 16, 32, 64)
+CFG4_TEMPLATES = 8  # distinct host weight sets per rank (adapters share them; every load still copies its bank)
+
+
+def module_keys(layers: int):
+    proj = {"q": "self_attn.q_proj", "k": "self_attn.k_proj", "v": "self_attn.v_proj", "o": "self_attn.o_proj",
+            "gate": "mlp.gate_proj", "up": "mlp.up_proj", "down": "mlp.down_proj"}
+    return {(l, n): f"layers.{l}.{proj[n]}" for l in range(layers) for n in proj}
+
+
+def run_pool_workload(args, wl: Workload, dev) -> None:
+    """cfg4: every step admits tokens, makes their adapters resident in the
+    64-slot pool (LRU eviction, pinned-host loads on the copy stream), writes
+    the routing and replays the graph of the 32-layer LoRA forward. Timed end
+    to end (loads included) with CUDA events and the host clock."""
+    import numpy as np
+
+    from multi_lora_b200 import _native
+    from multi_lora_b200.backend import CudaLoRABackend
+    from multi_lora_b200.batch_info import (BatchLoRAInfo, empty_kernel_input_metadata, group_rows,
+                                            write_kernel_input_metadata)
+    from multi_lora_b200.pool import LoRAMemoryPool
+    from multi_lora_b200.weights import AdapterWeights
+
+    dt = torch.bfloat16
+    keys = module_keys(wl.layers)
+    dims = {n: (i, o) for n, i, o, _ in wl.projs}
+    sum_in = sum(dims[n][0] for _, n in keys)
+    sum_out = sum(dims[n][1] for _, n in keys)
+    g = torch.Generator(device=dev).manual_seed(4321)
+    templates = {}
+    for r in CFG4_RANKS:
+        templates[r] = []
+        for _ in range(CFG4_TEMPLATES):
+            a_all = ((torch.rand(r, sum_in, generator=g, device=dev) * 2 - 1) / 64).to(dt).cpu()
+            b_all = (torch.randn(sum_out, r, generator=g, device=dev) * 0.02).to(dt).cpu()
+            mods, ia, ob = {}, 0, 0
+            for (l, n), key in keys.items():
+                i, o = dims[n]
+                mods[key] = (a_all[:, ia:ia + i], b_all[ob:ob + o])
+                ia += i
+                ob += o
+            templates[r].append(AdapterWeights(rank=r, scaling=2.0, modules=mods))
+    rng = np.random.default_rng(0)
+    ranks = rng.choice(CFG4_RANKS, size=wl.adapters)
+    store = {f"a{i}": templates[int(ranks[i])][i % CFG4_TEMPLATES] for i in range(wl.adapters)}
+    bank_bytes = {r: r * (sum_in + sum_out) * 2 for r in CFG4_RANKS}
+
+    pool = LoRAMemoryPool(POOL_SLOTS, wl.rank, dev, dtype=dt)
+    pool.ensure_buffers(templates[64][0])
+    T = wl.tokens
+    layers = []
+    gl = torch.Generator(device=dev).manual_seed(99)
+    for l in range(wl.layers):
+        L = Layer()
+        L.A, L.B, L.y = {}, {}, {}
+        for n, i, o, _ in wl.projs:
+            L.A[n], L.B[n] = pool.get_module_buffers(keys[(l, n)])
+            L.y[n] = torch.randn(T, o, generator=gl, device=dev).to(dt)
+        H = wl.hidden
+        L.h1 = torch.randn(T, H, generator=gl, device=dev).to(dt)
+        L.h2 = torch.randn(T, H, generator=gl, device=dev).to(dt)
+        L.w1 = (1 + 0.1 * torch.randn(H, generator=gl, device=dev)).to(dt)
+        L.w2 = (1 + 0.1 * torch.randn(H, generator=gl, device=dev)).to(dt)
+        L.xn1 = torch.empty(T, H, device=dev, dtype=dt)
+        L.xn2 = torch.empty(T, H, device=dev, dtype=dt)
+        xo = torch.randn(T, H, generator=gl, device=dev).to(dt)
+        xd = torch.randn(T, wl.inter, generator=gl, device=dev).to(dt)
+        L.x = {"q": L.xn1, "k": L.xn1, "v": L.xn1, "o": xo, "gate": L.xn2, "up": L.xn2, "down": xd}
+        layers.append(L)
+
+    # Zipf(s) over the adapters; admission in draw order until 64 distinct, the rest deferred
+    p_zipf = 1.0 / np.arange(1, wl.adapters + 1) ** ZIPF_S
+    p_zipf /= p_zipf.sum()
+    pending: list = []
+
+    def next_batch():
+        nonlocal pending
+        draws = list(rng.choice(wl.adapters, size=T - len(pending), p=p_zipf))
+        queue = pending + [f"a{int(i)}" for i in draws]
+        admitted, keep, distinct = [], [], set()
+        for nm in queue:
+            if nm in distinct or len(distinct) < POOL_SLOTS:
+                distinct.add(nm)
+                admitted.append(nm)
+            else:
+                keep.append(nm)
+        pending = keep
+        return admitted, distinct
+
+    be = CudaLoRABackend()
+    meta = empty_kernel_input_metadata(device=dev, dtype=dt)
+    stats = {"tokens": 0, "loads": 0, "h2d_bytes": 0, "distinct": 0, "steps": 0, "scatters": 0}
+
+    def schedule(count: bool):
+        nonlocal meta
+        admitted, distinct = next_batch()
+        before = set(pool.name_to_slot)
+        pool.prepare_lora_batch(distinct, weight_store=store)
+        new = [n for n in distinct if n not in before]
+        names, lens = group_rows(admitted, [])
+        info = pool.build_batch_info(names)
+        pad = T - len(names)  # fixed segment capacity: empty segments past the batch
+        padded = BatchLoRAInfo(weight_indices=list(info.weight_indices) + [0] * pad, lora_ranks=info.lora_ranks,
+                               scalings=info.scalings)
+        meta = write_kernel_input_metadata(meta, padded, device=dev, dtype=dt, seq_lens=list(lens) + [0] * pad)
+        be.set_kernel_input_metadata(meta)
+        if count:
+            stats["tokens"] += len(admitted)
+            stats["loads"] += len(new)
+            per_rank: dict = {}
+            for n in new:
+                per_rank[store[n].rank] = per_rank.get(store[n].rank, 0) + 1
+            stats["scatters"] += sum((c + 3) // 4 for c in per_rank.values())  # one launch per 4 banks
+            stats["h2d_bytes"] += sum(bank_bytes[store[n].rank] for n in new)
+            stats["distinct"] += len(distinct)
+            stats["steps"] += 1
+
+    schedule(False)
+    step_graph = capture(lambda: run_step(wl, layers, be))
+    path = _native.capi().mlora_last_apply_path()
+    per_layer = launches_per_layer(wl, True, path, 1)
+    launches = wl.layers * (per_layer["lora"] + per_layer["rmsnorm"])
+    for _ in range(max(args.warmup, 3)):  # fills the pool
+        schedule(False)
+        step_graph.replay()
+    torch.cuda.synchronize()
+    visible = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+    clocks = ClockSampler(visible[0].strip() if visible else 0)
+    clocks.start()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    e0.record(st)
+    for _ in range(args.steps):
+        schedule(True)
+        step_graph.replay()
+    e1.record(st)
+    torch.cuda.synchronize()
+    wall_ms = (time.perf_counter() - t0) * 1e3
+    clk = clocks.stop()
+    ms = max(e0.elapsed_time(e1), wall_ms) / args.steps
+    g_c = capture(lambda: run_step(wl, layers, be))  # compute alone, the last step's routing
+    compute_ms = time_graph(g_c, 20)
+    del g_c
+    pool.buffers.check_status()
+    be.check_routing()
+    value = stats["tokens"] / (ms * args.steps / 1e3)
+    per_step_h2d = stats["h2d_bytes"] / args.steps
+    out = {"metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+           "vs_baseline": None, "dtype": "bf16",
+           "data": "synthetic (seeded; 8 distinct host weight sets per rank shared by the 256 adapters)",
+           "config": {"workload": wl.desc, "global_batch": T, "seq_len": 1, "layers": wl.layers,
+                      "adapters": wl.adapters, "pool_slots": POOL_SLOTS, "max_rank": wl.rank,
+                      "parallelism": "single", "l2": "no flush: GBs of pool weights and host loads per step"},
+           "pool": {"tokens_per_step": round(stats["tokens"] / args.steps, 1),
+                    "distinct_adapters_per_step": round(stats["distinct"] / args.steps, 1),
+                    "loads_per_step": round(stats["loads"] / args.steps, 2),
+                    "h2d_gb_per_step": round(per_step_h2d / 1e9, 3),
+                    "h2d_gbs_achieved": round(per_step_h2d / (ms / 1e3) / 1e9, 1),
+                    "compute_ms_per_step_alone": round(compute_ms, 4), "deferred_at_end": len(pending)},
+           "e2e": {"value": round(value, 1), "unit": UNIT, "h2d_bytes_per_step": round(per_step_h2d),
+                   "d2h_bytes_per_step": 0, "path": "admission + pool.prepare_lora_batch (evict, pinned H2D, "
+                                                    "scatter) + routing write + graph replay, every step"},
+           "gpu_launches": launches * args.steps + stats["scatters"], "clocks": clk, "pdl": _native.get_pdl(),
+           "apply_path": APPLY_PATH_NAMES.get(path, str(path))}
+    print(json.dumps(out), flush=True)
+    del step_graph
+
+
 def config_block(wl: Workload, n: int) -> dict:
     return {"workload": wl.desc, "global_batch": wl.tokens, "seq_len": 1, "layers": wl.layers,
             "adapters": wl.adapters, "rank": wl.rank,
@@ -412,6 +590,14 @@ def main() -> None:
                                           f"x{wl.layers} layers"},
                "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(out), flush=True)
+        return
+
+    if wl.name == "cfg4":
+        if world > 1:
+            raise SystemExit("cfg4 is a single-GPU workload (one slot pool per GPU)")
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        run_pool_workload(args, wl, dev)
         return
 
     tp = world

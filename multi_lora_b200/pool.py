@@ -105,6 +105,10 @@ class _GpuBuffers:
         self.release_modules = True  # drop the per-module host tensors once banked
         self._stage: Optional[torch.Tensor] = None
         self._status: Optional[torch.Tensor] = None
+        # per slot: an event on the compute stream after the last work that may read it
+        self._slot_event: Dict[int, torch.cuda.Event] = {}
+        self._live_slots: Set[int] = set()
+        self._loaded: Set[int] = set()  # slots written at least once
 
     def ensure(self, weights: AdapterWeights) -> None:
         """Create zeroed slot stacks for modules seen for the first time."""
@@ -119,15 +123,38 @@ class _GpuBuffers:
             self.A[key] = torch.zeros((k, r, n_in), device=self.device, dtype=self.dtype)
             self.B[key] = torch.zeros((k, n_out, r), device=self.device, dtype=self.dtype)
 
+    def begin_batch(self, slots: Set[int]) -> None:
+        """A new batch is being prepared: everything enqueued on the compute
+        stream so far may read the previous batch's slots, so stamp them with
+        an event there; ``slots`` are the new batch's."""
+        if self.routing_only:
+            return
+        if self._live_slots:
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream(self.device))
+            for s in self._live_slots:
+                self._slot_event[s] = ev
+        self._live_slots = set(slots)
+
     def write_many(self, pairs: List[Tuple[int, AdapterWeights]]) -> None:
-        """Load ``[(slot, weights), ...]`` into their slots (async on the copy stream)."""
+        """Load ``[(slot, weights), ...]`` into their slots (async on the copy stream).
+
+        The copy stream waits only for the compute that last read the target
+        slots (their events), not for all queued compute, so a load into a slot
+        the previous batch did not use overlaps that batch's kernels.
+        """
         if not pairs or self.routing_only:
             return
         if self._copy_stream is None:
             self._copy_stream = torch.cuda.Stream(device=self.device)
             self._load_event = torch.cuda.Event()
-        # slots may still be read by queued compute: start after it
-        self._copy_stream.wait_stream(torch.cuda.current_stream(self.device))
+        for slot, _ in pairs:
+            ev = self._slot_event.get(slot)
+            if ev is not None:
+                self._copy_stream.wait_event(ev)
+            elif slot in self._loaded:  # written before, outside prepared batches: wait for all queued compute
+                self._copy_stream.wait_stream(torch.cuda.current_stream(self.device))
+        self._loaded.update(slot for slot, _ in pairs)
         with torch.cuda.stream(self._copy_stream):
             self._load_flat(pairs)
         self._load_event.record(self._copy_stream)
@@ -294,6 +321,7 @@ class LoRAMemoryPool:
             self.buffers.ensure(w)
             self._slot_rank_scaling[slot] = (w.rank, w.scaling)
             pairs.append((slot, w))
+        self.buffers.begin_batch({self.name_to_slot[n] for n in lora_names})
         self.buffers.write_many(pairs)
         self.buffers.wait_load()
 

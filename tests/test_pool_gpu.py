@@ -101,3 +101,40 @@ def test_load_overlaps_on_copy_stream_and_compute_waits(cuda_dev):
     torch.cuda.synchronize()
     assert torch.equal(first.cpu(), ref.modules["big"][0])
     assert pool.buffers._copy_stream is not None
+
+
+def test_load_into_evicted_slot_waits_for_queued_reads(cuda_dev):
+    """A load into a slot the previous batch used starts only after the compute
+    queued before the new batch was prepared (per-slot event), so that compute
+    still sees the old adapter."""
+    pool = LoRAMemoryPool(2, 8, cuda_dev, torch.bfloat16)
+    seeds = {"a": 1, "b": 2, "c": 3}
+    store = {n: _weights(MODULES, 8, ["big"], s, torch.bfloat16) for n, s in seeds.items()}
+    refs = {n: _weights(MODULES, 8, ["big"], s, torch.bfloat16) for n, s in seeds.items()}
+    pool.ensure_buffers(store["a"])
+    pool.prepare_lora_batch({"a", "b"}, weight_store=store)
+    slot_a = pool.get_slot_id("a")
+    torch.cuda._sleep(100_000_000)  # bounded busy wait: the read below is still queued at the next prepare
+    a, _ = pool.get_slot_weights(slot_a, "big")
+    seen = a[:8].clone()
+    pool.prepare_lora_batch({"b", "c"}, weight_store=store)  # evicts a; c goes into its slot
+    assert pool.get_slot_id("c") == slot_a
+    torch.cuda.synchronize()
+    assert torch.equal(seen.cpu(), refs["a"].modules["big"][0])
+    a2, _ = pool.get_slot_weights(slot_a, "big")
+    assert torch.equal(a2[:8].cpu(), refs["c"].modules["big"][0])
+    pool.buffers.check_status()
+
+
+def test_load_into_unused_slot_overlaps_queued_compute(cuda_dev):
+    """Slots no queued work reads are loaded without waiting for the compute stream."""
+    pool = LoRAMemoryPool(2, 8, cuda_dev, torch.bfloat16)
+    store = {"a": _weights(MODULES, 8, ["big"], 1, torch.bfloat16)}
+    pool.ensure_buffers(store["a"])
+    torch.cuda.synchronize()
+    torch.cuda._sleep(400_000_000)  # bounded busy wait (~0.2 s) on the compute stream
+    pool.prepare_lora_batch({"a"}, weight_store=store)
+    pool.buffers._load_event.synchronize()  # the load finished ...
+    overlapped = not torch.cuda.current_stream().query()  # ... while the queued compute still runs
+    torch.cuda.synchronize()
+    assert overlapped
