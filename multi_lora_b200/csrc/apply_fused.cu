@@ -9,13 +9,14 @@
 //
 // Layout on the GPU: one thread-block CLUSTER per (adapter slot, projection),
 // CS = 8 or 16 CTAs. CTA j of the cluster
-//   1. owns k-slice j of the input dim: one thread issues TMA bulk copies of
-//      A[slot, :rank, slice] and of its output block B[slot, block, :rank] into
-//      shared memory (an mbarrier counts the bytes) BEFORE
-//      griddepcontrol.wait, so under programmatic dependent launch the weight
-//      stream overlaps the previous kernel;
-//   2. after the wait it bulk-copies the slot's x rows (its slice) and y rows
-//      (its output block) and computes split-K partials of mid with warp-level
+//   1. owns k-slice j of the input dim: its threads copy A[slot, :rank, slice]
+//      into padded shared-memory rows with 16-byte cp.async pieces, and one
+//      thread copies its output block B[slot, block, :rank] with one TMA bulk
+//      copy (an mbarrier counts the bytes), BEFORE griddepcontrol.wait, so
+//      under programmatic dependent launch the weight stream overlaps the
+//      previous kernel;
+//   2. after the wait it loads the slot's x rows (its slice) and y rows (its
+//      output block) and computes split-K partials of mid with warp-level
 //      tensor-core tiles (mma.sync m16n8k16: up to 8 tokens per tile cost the
 //      same as one, where a scalar loop would grow with the token count);
 //   3. pushes its partials into every peer CTA's shared memory with st.async
@@ -137,7 +138,7 @@ __global__ void __launch_bounds__(kFusedNT) apply_fused_kernel(const FusedArgs p
   __shared__ int s_rows[TT];
   __shared__ __align__(16) float s_part[TT][RM];
   __shared__ __align__(16) T s_mid[16][MP];
-  __shared__ __align__(8) uint64_t bar_w, bar_x, bar_p;
+  __shared__ __align__(8) uint64_t bar_w, bar_p;
   extern __shared__ __align__(128) unsigned char s_dyn[];
 
   cg::cluster_group cluster = cg::this_cluster();
@@ -198,7 +199,6 @@ __global__ void __launch_bounds__(kFusedNT) apply_fused_kernel(const FusedArgs p
   // ---- prologue: adapter weights (stable for the step) into shared memory ----
   if (tid == 0) {
     mbar_init(&bar_w, 1);
-    mbar_init(&bar_x, 1);
     mbar_init(&bar_p, 1);
     fence_barrier_init();
   }
@@ -210,14 +210,21 @@ __global__ void __launch_bounds__(kFusedNT) apply_fused_kernel(const FusedArgs p
   const T* __restrict__ a_src = static_cast<const T*>(m.a) + (int64_t)slot * R * p.in_dim + k0;
   const T* __restrict__ b_src = static_cast<const T*>(m.b) + ((int64_t)slot * m.out_dim + o_lo) * R;
   const bool b_dense = rank == R;  // B rows hold exactly the rank: one contiguous block
+  // Weights: the contiguous B block as ONE bulk copy (rank == max_rank); the
+  // A rows (and a B block with stale columns) as 16-byte cp.async pieces over
+  // every thread -- a 1-D bulk copy costs ~80-100 ns of issue time, so one
+  // thread issuing a copy per A row put ~1.5 us on the critical path.
   if (tid == 0) {
-    const uint32_t a_bytes = (uint32_t)rank * klen * sizeof(T);
     const uint32_t b_bytes = b_dense ? (uint32_t)olen * R * sizeof(T) : 0u;
-    mbar_arrive_expect_tx(&bar_w, a_bytes + b_bytes);
-    if (klen > 0)
-      for (int n = 0; n < rank; ++n)
-        bulk_copy_g2s(s_a + (size_t)n * kp, a_src + (int64_t)n * p.in_dim, klen * sizeof(T), &bar_w);
+    mbar_arrive_expect_tx(&bar_w, b_bytes);
     if (b_bytes > 0) bulk_copy_g2s(s_b, b_src, b_bytes, &bar_w);
+  }
+  {
+    const int kc8 = klen / 8;
+    for (int e = tid; e < rank * kc8; e += NT) {
+      const int n = e / kc8, c = e - n * kc8;
+      cp_async16(s_a + (size_t)n * kp + c * 8, a_src + (int64_t)n * p.in_dim + c * 8);
+    }
   }
   const int rc = (rank + 7) / 8;  // 16-byte B chunks per row that hold rank columns
   if (!b_dense) {  // rows of R with only `rank` valid columns: 16-byte copies per thread
@@ -226,6 +233,7 @@ __global__ void __launch_bounds__(kFusedNT) apply_fused_kernel(const FusedArgs p
       cp_async16(s_b + (size_t)row * R + c * 8, b_src + (int64_t)row * R + c * 8);
     }
   }
+  cp_async_commit();  // group: this CTA's weights
   pdl_trigger();
   pdl_wait();  // x and y come from earlier kernels
 
@@ -235,7 +243,7 @@ __global__ void __launch_bounds__(kFusedNT) apply_fused_kernel(const FusedArgs p
   const uint32_t smid_addr = smem_addr(&s_mid[0][0]);
   const int g = lane >> 2, cq = lane & 3;
   bool ok = true;
-  uint32_t x_phase = 0, p_phase = 0;
+  uint32_t p_phase = 0;
   bool first = true;
   for (int from = 0; from < p.bs; from += kFusedScan) {
     if (from > 0) {
@@ -250,13 +258,14 @@ __global__ void __launch_bounds__(kFusedNT) apply_fused_kernel(const FusedArgs p
       if (klen % 16 != 0)
         for (int e = tid; e < TT * 8; e += NT) s_x[(size_t)(e / 8) * kp + klen + (e % 8)] = Num<T>::from_f(0.f);
       __syncthreads();
-      if (tid == 0 && m.y_tma && olen > 0) {  // this tile's y rows (output block); needed only by the expand
-        fence_proxy_async_smem();
-        mbar_arrive_expect_tx(&bar_x, (uint32_t)nt * olen * sizeof(T));
-        for (int t = 0; t < nt; ++t)
-          bulk_copy_g2s(s_y + (size_t)t * p.ob_max, ybase + (int64_t)s_rows[t] * m.y_stride + o_lo, olen * sizeof(T),
-                        &bar_x);
+      if (m.y_tma && olen > 0) {  // this tile's y rows (output block), needed only by the expand
+        const int oc8 = olen / 8;
+        for (int e = tid; e < nt * oc8; e += NT) {
+          const int t = e / oc8, c = e - t * oc8;
+          cp_async16(s_y + (size_t)t * p.ob_max + c * 8, ybase + (int64_t)s_rows[t] * m.y_stride + o_lo + c * 8);
+        }
       }
+      cp_async_commit();  // group: this tile's y rows (possibly empty)
       {  // this tile's x rows (k-slice): plain 16-byte loads by every thread (L2 hits)
         const int kc = klen / 8;
         for (int e = tid; e < nt * kc; e += NT) {
@@ -265,11 +274,12 @@ __global__ void __launch_bounds__(kFusedNT) apply_fused_kernel(const FusedArgs p
           *reinterpret_cast<uint4*>(s_x + (size_t)t * kp + c * 8) = v;
         }
       }
-      if (first) ok = mbar_wait(&bar_w, 0, p.status) && ok;
-      __syncthreads();  // x tile complete
+      if (first) {
+        cp_async_wait<1>();  // the weights group (this tile's y group may still be in flight)
+        ok = mbar_wait(&bar_w, 0, p.status) && ok;
+      }
+      __syncthreads();  // x tile and weights complete
       if (first && !b_dense) {  // B block: zero the stale columns past the rank once it has landed
-        cp_async_wait_all();
-        __syncthreads();
         for (int e = tid; e < olen * (R - rank); e += NT) {
           const int row = e / (R - rank), c = rank + e % (R - rank);
           s_b[(size_t)row * R + c] = Num<T>::from_f(0.f);
@@ -348,8 +358,8 @@ __global__ void __launch_bounds__(kFusedNT) apply_fused_kernel(const FusedArgs p
       }
       __syncthreads();  // s_mid complete
       if (m.y_tma && olen > 0) {  // y rows staged during the shrink and exchange
-        ok = mbar_wait(&bar_x, x_phase, p.status) && ok;
-        x_phase ^= 1u;
+        cp_async_wait<0>();
+        __syncthreads();
       }
       // ---- expand: this CTA's output block on tensor cores, fused scaling + residual ----
       if (ok) {
@@ -405,12 +415,9 @@ __global__ void __launch_bounds__(kFusedNT) apply_fused_kernel(const FusedArgs p
   if (first) {
     cluster_wait_acquire();  // pairs the prologue arrive
     mbar_wait(&bar_w, 0, p.status);
-    if (!b_dense) cp_async_wait_all();
   }
-  if (!ok && tid == 0) {  // ok is only cleared inside a tile
-    if (m.y_tma && olen > 0) mbar_wait(&bar_x, x_phase ^ 1u, p.status);
-    mbar_wait(&bar_p, p_phase ^ 1u, p.status);
-  }
+  cp_async_wait<0>();
+  if (!ok && tid == 0) mbar_wait(&bar_p, p_phase ^ 1u, p.status);  // ok is only cleared inside a tile
 }
 
 namespace {
