@@ -221,7 +221,7 @@ int apply_impl(const void* x, int64_t rows, int64_t in_dim, int64_t x_row_stride
   // (one launch, shorter dependency chain: 2.2x faster at 64 tokens x 32 adapters).
   // Long segments (prefill) go to the tensor-core kernels when the shape fits them.
   const bool tc_pref = forced == 4 || (forced == 0 && meta->max_len >= 64);
-  bool tcable = tc_pref && es == 2 && max_rank == 64 && in_dim % 64 == 0 && x != nullptr && aligned(x, 16) &&
+  bool tcable = tc_pref && es == 2 && (max_rank == 16 || max_rank == 32 || max_rank == 64) && in_dim % 64 == 0 && x != nullptr && aligned(x, 16) &&
                 x_row_stride % 8 == 0 && mid != nullptr && aligned(mid, 16) && mid_row_stride % 8 == 0 &&
                 mid_row_stride >= (int64_t)n * max_rank && (mids == nullptr || mids[0] == mid) && rows <= INT32_MAX;
   for (int i = 0; i < n && tcable; ++i)

@@ -9,7 +9,7 @@
 // Each segment's rows are cut into tiles of 128 tokens (the last one ragged;
 // rows past the segment are computed but never stored).
 //   lora_shrink_tc_kernel: one CTA per (tile, K split). TMA streams 64-column blocks of x
-//     (128 x 64) and of every projection's A[slot] (R x 64, R = 64) through a
+//     (128 x 64) and of every projection's A[slot] (R x 64) through a
 //     3-4 stage ring in the 128-byte-swizzled K-major layout; one thread issues
 //     tcgen05.mma (M = 128, N = n_proj * 64, K = 16) into a TMEM accumulator;
 //     every stage is released by tcgen05.commit. The epilogue reads TMEM row
@@ -23,7 +23,7 @@
 //     tcgen05.mma (K = 64) fill a 128 x 128 TMEM accumulator; the epilogue
 //     fuses the scaling, the rounding and the residual add and stores the
 //     segment's rows with 16-byte stores.
-// Shapes: bf16/f16, max_rank 64, in % 64 == 0, out % 8 == 0. Adapter weights
+// Shapes: bf16/f16, max_rank 16, 32 or 64, in % 64 == 0, out % 8 == 0. Adapter weights
 // are requested before griddepcontrol.wait; x, mid and y after it. Waits are
 // bounded; TMEM is always freed.
 #include <mutex>
@@ -38,7 +38,8 @@ constexpr int kTcThreads = 128;
 constexpr int kTcTileM = 128;  // tokens per tile
 constexpr int kTcBK = 64;      // K block (one 128-byte swizzle row)
 constexpr int kTcBN = 128;     // expand output columns per CTA
-constexpr int kTcR = 64;       // max_rank handled by these kernels
+// max_rank RT in {16, 32, 64}: rank-wide tiles (mid, B) have rows of RT * 2
+// bytes, swizzled with that span (32B / 64B / 128B).
 
 struct TcTile {
   int seg, row0, rows, slot, rank;
@@ -102,10 +103,10 @@ __device__ __forceinline__ const CUtensorMap* tc_map(const CUtensorMap* maps, in
 // ---------------------------------------------------------------------------
 // shrink: mid[tile rows, m*R : m*R + rank] for every projection m
 // ---------------------------------------------------------------------------
-template <typename T>
+template <typename T, int RT>
 __global__ void __launch_bounds__(kTcThreads) lora_shrink_tc_kernel(const __grid_constant__ PrefillArgs p) {
   constexpr uint32_t X_BYTES = kTcTileM * kTcBK * 2;  // 16 KB
-  constexpr uint32_t A_BYTES = kTcR * kTcBK * 2;      // 8 KB per projection
+  constexpr uint32_t A_BYTES = RT * kTcBK * 2;        // RT rows of 128 B per projection
   extern __shared__ __align__(1024) unsigned char s_raw[];
   __shared__ __align__(8) uint64_t full[4], empty[4], done;
   __shared__ uint32_t s_tmem;
@@ -133,7 +134,8 @@ __global__ void __launch_bounds__(kTcThreads) lora_shrink_tc_kernel(const __grid
   const int splits = gridDim.x, split = blockIdx.x;
   const int ns = p.tc_stages;
   const uint32_t stage_bytes = X_BYTES + (uint32_t)nm * A_BYTES;
-  const uint32_t ncols = nm == 1 ? 64u : nm == 2 ? 128u : 256u;
+  const int N = nm * RT;  // MMA N: the projections' rank rows side by side
+  const uint32_t ncols = N <= 32 ? 32u : N <= 64 ? 64u : N <= 128 ? 128u : 256u;
   if (tid == 0) {
     for (int s = 0; s < ns; ++s) {
       mbar_init(&full[s], 1);
@@ -177,7 +179,7 @@ __global__ void __launch_bounds__(kTcThreads) lora_shrink_tc_kernel(const __grid
       }
     }
   } else if (tid == 32) {  // ---- MMA issuer ----
-    const uint32_t idesc = umma_idesc_f16(Num<T>::is_bf16, kTcTileM, nm * kTcR);
+    const uint32_t idesc = umma_idesc_f16(Num<T>::is_bf16, kTcTileM, N);
     for (int kb = 0; kb < KB && ok; ++kb) {
       const int s = kb % ns;
       ok = mbar_wait(&full[s], (kb / ns) & 1, p.status);
@@ -200,15 +202,16 @@ __global__ void __launch_bounds__(kTcThreads) lora_shrink_tc_kernel(const __grid
     // ---- split K: fp32 partials into this CTA's shared memory (the ring is
     // idle now), then each CTA of the cluster sums the splits, in split order,
     // for its share of the rows and writes them ----
-    const int N = nm * kTcR, PS = N + 4;  // padded row (conflict-free 16-byte stores)
+    const int PS = N + 4;  // padded row (conflict-free 16-byte stores)
     float* part = reinterpret_cast<float*>(smem);
-    for (int c = 0; c < N / 32; ++c) {
+    for (int c = 0; c < (N + 31) / 32; ++c) {
       float v[32];
       tmem_ld32(taddr + ((uint32_t)(warp * 32) << 16) + (uint32_t)(c * 32), v);
 #pragma unroll
       for (int q = 0; q < 8; ++q)
-        *reinterpret_cast<float4*>(part + r * PS + c * 32 + 4 * q) =
-            make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        if (c * 32 + 4 * q < N)
+          *reinterpret_cast<float4*>(part + r * PS + c * 32 + 4 * q) =
+              make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
     }
     tc_fence_before();
     cluster_arrive_release();
@@ -229,7 +232,7 @@ __global__ void __launch_bounds__(kTcThreads) lora_shrink_tc_kernel(const __grid
         acc.w += v.w;
       }
       if (fin && row < t.rows) {
-        const int m = c4 / kTcR, k = c4 % kTcR;
+        const int m = c4 / RT, k = c4 % RT;
         T* dst = static_cast<T*>(p.mid) + (int64_t)(t.row0 + row) * p.mid_stride + m * p.R + k;
         const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
 #pragma unroll
@@ -247,26 +250,27 @@ __global__ void __launch_bounds__(kTcThreads) lora_shrink_tc_kernel(const __grid
   // ---- epilogue: thread = token row; round once to T; columns < rank only ----
   const bool row_ok = fin && r < t.rows;
   T* mid = static_cast<T*>(p.mid) + (int64_t)(t.row0 + r) * p.mid_stride;
-  for (int m = 0; m < nm; ++m) {
-    for (int h = 0; h < kTcR / 32; ++h) {
-      float v[32];
-      tmem_ld32(taddr + ((uint32_t)(warp * 32) << 16) + (uint32_t)(m * kTcR + h * 32), v);
-      if (row_ok) {
-        T* dst = mid + m * p.R + h * 32;
-        if (t.rank >= h * 32 + 32) {
+  for (int c = 0; c < (N + 31) / 32; ++c) {
+    float v[32];
+    tmem_ld32(taddr + ((uint32_t)(warp * 32) << 16) + (uint32_t)(c * 32), v);
+    if (row_ok) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint4 u;
-            u.x = Pack2<T>::pack(Num<T>::from_f(v[8 * q + 0]), Num<T>::from_f(v[8 * q + 1]));
-            u.y = Pack2<T>::pack(Num<T>::from_f(v[8 * q + 2]), Num<T>::from_f(v[8 * q + 3]));
-            u.z = Pack2<T>::pack(Num<T>::from_f(v[8 * q + 4]), Num<T>::from_f(v[8 * q + 5]));
-            u.w = Pack2<T>::pack(Num<T>::from_f(v[8 * q + 6]), Num<T>::from_f(v[8 * q + 7]));
-            *reinterpret_cast<uint4*>(dst + 8 * q) = u;
-          }
+      for (int q = 0; q < 4; ++q) {  // 8 columns at a time; RT is a multiple of 16
+        const int col = c * 32 + 8 * q;
+        if (col >= N) continue;
+        const int m = col / RT, k = col % RT;
+        T* dst = mid + m * p.R + k;
+        if (k + 8 <= t.rank) {
+          uint4 u;
+          u.x = Pack2<T>::pack(Num<T>::from_f(v[8 * q + 0]), Num<T>::from_f(v[8 * q + 1]));
+          u.y = Pack2<T>::pack(Num<T>::from_f(v[8 * q + 2]), Num<T>::from_f(v[8 * q + 3]));
+          u.z = Pack2<T>::pack(Num<T>::from_f(v[8 * q + 4]), Num<T>::from_f(v[8 * q + 5]));
+          u.w = Pack2<T>::pack(Num<T>::from_f(v[8 * q + 6]), Num<T>::from_f(v[8 * q + 7]));
+          *reinterpret_cast<uint4*>(dst) = u;
         } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (h * 32 + i < t.rank) dst[i] = Num<T>::from_f(v[i]);
+          for (int i = 0; i < 8; ++i)
+            if (k + i < t.rank) dst[i] = Num<T>::from_f(v[8 * q + i]);
         }
       }
     }
@@ -279,10 +283,11 @@ __global__ void __launch_bounds__(kTcThreads) lora_shrink_tc_kernel(const __grid
 // ---------------------------------------------------------------------------
 // expand: y[tile rows, block] = T(T(scale * mid @ B^T) + y)
 // ---------------------------------------------------------------------------
-template <typename T>
+template <typename T, int RT>
 __global__ void __launch_bounds__(kTcThreads) lora_expand_tc_kernel(const __grid_constant__ PrefillArgs p) {
-  constexpr uint32_t M_BYTES = kTcTileM * kTcR * 2;   // mid tile 16 KB
-  constexpr uint32_t B_BYTES = kTcBN * kTcR * 2;      // 16 KB
+  constexpr int RB = RT * 2;                          // bytes per rank-wide row (= swizzle span)
+  constexpr uint32_t M_BYTES = kTcTileM * RB;         // mid tile
+  constexpr uint32_t B_BYTES = kTcBN * RB;            // B block
   constexpr uint32_t Y_BYTES = kTcTileM * kTcBK * 2;  // one 64-column y box, 16 KB
   extern __shared__ __align__(1024) unsigned char s_raw[];
   __shared__ __align__(8) uint64_t bar_load, bar_mma;
@@ -338,12 +343,12 @@ __global__ void __launch_bounds__(kTcThreads) lora_expand_tc_kernel(const __grid
     tma_load_2d(s_y + Y_BYTES, tc_map(p.y_map, m), n0 + kTcBK, t.row0, &bar_load);
   }
   bool ok = mbar_wait(&bar_load, 0, p.status);
-  if (t.rank < kTcR) {  // columns >= rank of mid (stale) and of B (stale) contribute zero
-    const int w = kTcR - t.rank;
+  if (t.rank < RT) {  // columns >= rank of mid (stale) and of B (stale) contribute zero
+    const int w = RT - t.rank;
     for (int e = tid; e < kTcTileM * w; e += kTcThreads) {
       const int row = e / w, col = t.rank + e % w;
-      *reinterpret_cast<T*>(s_mid + sw128_offset(row, col)) = Num<T>::from_f(0.f);
-      *reinterpret_cast<T*>(s_b + sw128_offset(row, col)) = Num<T>::from_f(0.f);  // kTcBN == kTcTileM rows
+      *reinterpret_cast<T*>(s_mid + sw_offset(row, col, RB)) = Num<T>::from_f(0.f);
+      *reinterpret_cast<T*>(s_b + sw_offset(row, col, RB)) = Num<T>::from_f(0.f);  // kTcBN == kTcTileM rows
     }
     fence_proxy_async_smem();
   }
@@ -351,9 +356,9 @@ __global__ void __launch_bounds__(kTcThreads) lora_expand_tc_kernel(const __grid
   if (tid == 0 && ok) {
     tc_fence_after();
     const uint32_t idesc = umma_idesc_f16(Num<T>::is_bf16, kTcTileM, kTcBN);
-    const uint64_t ad = umma_desc_sw128(s_mid), bd = umma_desc_sw128(s_b);
+    const uint64_t ad = umma_desc_kmajor(s_mid, RB), bd = umma_desc_kmajor(s_b, RB);
 #pragma unroll
-    for (int k = 0; k < kTcR / 16; ++k) umma_f16(taddr, ad + 2 * k, bd + 2 * k, idesc, k != 0);
+    for (int k = 0; k < RT / 16; ++k) umma_f16(taddr, ad + 2 * k, bd + 2 * k, idesc, k != 0);
     umma_commit(&bar_mma);
   }
   __syncwarp();
@@ -421,19 +426,22 @@ EncodeTiled encoder() {
 }
 
 // 2-D map over a row-major [outer, inner] matrix with rows `stride_elems` apart;
-// box {64, box_rows}, 128-byte swizzle, zero fill out of bounds.
+// box {box_inner, box_rows}, swizzled with the box row's span (32, 64 or 128
+// bytes), zero fill out of bounds.
 bool encode_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, uint64_t outer, uint64_t stride_elems,
-               uint32_t box_rows) {
+               uint32_t box_inner, uint32_t box_rows) {
   EncodeTiled enc = encoder();
   if (enc == nullptr) return false;
   const cuuint64_t dims[2] = {inner, outer};
   const cuuint64_t strides[1] = {stride_elems * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)kTcBK, box_rows};
+  const cuuint32_t box[2] = {box_inner, box_rows};
   const cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapSwizzle sw = box_inner * 2 == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : box_inner * 2 == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                      : CU_TENSOR_MAP_SWIZZLE_32B;
   return enc(map, dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
-             const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+             const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 long long tc_sm_count() {
@@ -459,23 +467,24 @@ bool ensure_smem_tc(K kern, int bytes) {
   return true;
 }
 
-template <typename T>
-cudaError_t launch_prefill_t(PrefillArgs& a, int dtype, cudaStream_t st, bool pdl) {
+template <typename T, int RT>
+cudaError_t launch_prefill_t(PrefillArgs& a, cudaStream_t st, bool pdl) {
   const int nm = a.n_mod;
-  a.tc_stages = nm <= 2 ? 4 : 3;
-  const int shrink_smem = a.tc_stages * (kTcTileM * kTcBK * 2 + nm * kTcR * kTcBK * 2) + 1024;
-  const int expand_smem = (kTcTileM * kTcR * 2) + (kTcBN * kTcR * 2) + 2 * (kTcTileM * kTcBK * 2) + 1024;
-  auto ks = lora_shrink_tc_kernel<T>;
-  auto ke = lora_expand_tc_kernel<T>;
-  // largest shrink configuration: 3 stages of x + four projections' A blocks (4 stages of two are smaller)
-  static const bool smem_ok = ensure_smem_tc(ks, 3 * (kTcTileM * kTcBK * 2 + 4 * kTcR * kTcBK * 2) + 1024) &&
-                              ensure_smem_tc(ke, expand_smem);
+  a.tc_stages = nm * RT <= 128 ? 4 : 3;
+  const int shrink_smem = a.tc_stages * (kTcTileM * kTcBK * 2 + nm * RT * kTcBK * 2) + 1024;
+  const int expand_smem = (kTcTileM * RT * 2) + (kTcBN * RT * 2) + 2 * (kTcTileM * kTcBK * 2) + 1024;
+  auto ks = lora_shrink_tc_kernel<T, RT>;
+  auto ke = lora_expand_tc_kernel<T, RT>;
+  // the largest shrink configuration of this RT (3 or 4 stages of x + four projections' A blocks)
+  static const bool smem_ok =
+      ensure_smem_tc(ks, (4 * RT <= 128 ? 4 : 3) * (kTcTileM * kTcBK * 2 + 4 * RT * kTcBK * 2) + 1024) &&
+      ensure_smem_tc(ke, expand_smem);
   if (!smem_ok) return cudaErrorNotSupported;
   const long long tiles = (a.S + kTcTileM - 1) / kTcTileM + (long long)a.bs;
   if (tiles > 65535) return cudaErrorNotSupported;
   int blocks = 0;
   for (int m = 0; m < nm; ++m) blocks += (a.mod[m].out_dim + kTcBN - 1) / kTcBN;
-  // K splits: enough shrink CTAs for one per SM (one fits per SM), at least 4 K blocks each, a cluster of <= 8
+  // K splits: enough shrink CTAs for one per SM, at least 4 K blocks each, a cluster of <= 8
   int splits = (int)(tc_sm_count() / tiles);
   splits = splits < 1 ? 1 : splits > 8 ? 8 : splits;
   while (splits > 1 && a.in_dim / kTcBK < 4 * splits) --splits;
@@ -498,11 +507,19 @@ cudaError_t launch_prefill_t(PrefillArgs& a, int dtype, cudaStream_t st, bool pd
   return launch_kernel(ke, dim3((unsigned)blocks, (unsigned)tiles), dim3(kTcThreads), expand_smem, st, true, a);
 }
 
+template <typename T>
+cudaError_t launch_prefill_r(PrefillArgs& a, cudaStream_t st, bool pdl) {
+  return a.R == 16 ? launch_prefill_t<T, 16>(a, st, pdl)
+       : a.R == 32 ? launch_prefill_t<T, 32>(a, st, pdl)
+                   : launch_prefill_t<T, 64>(a, st, pdl);
+}
+
 }  // namespace
 
 cudaError_t launch_apply_prefill(const PrefillLaunch& l, int dtype, cudaStream_t st, bool pdl) {
   if (dtype != kBF16 && dtype != kF16) return cudaErrorNotSupported;
-  if (l.n_mod < 1 || l.n_mod > kMaxPrefillModules || l.R != kTcR || l.in_dim % kTcBK != 0) return cudaErrorNotSupported;
+  if (l.n_mod < 1 || l.n_mod > kMaxPrefillModules || l.in_dim % kTcBK != 0) return cudaErrorNotSupported;
+  if (l.R != 16 && l.R != 32 && l.R != 64) return cudaErrorNotSupported;
   PrefillArgs a{};
   a.n_mod = l.n_mod;
   a.mid = l.mid;
@@ -518,19 +535,20 @@ cudaError_t launch_apply_prefill(const PrefillLaunch& l, int dtype, cudaStream_t
   a.R = l.R;
   a.num_slots = l.num_slots;
   a.status = l.status;
-  bool ok = encode_2d(&a.x_map, l.x, dtype, (uint64_t)l.in_dim, (uint64_t)l.S, (uint64_t)l.x_stride, kTcTileM) &&
-            encode_2d(&a.mid_map, l.mid, dtype, (uint64_t)l.n_mod * l.R, (uint64_t)l.S, (uint64_t)l.mid_stride, kTcTileM);
+  const uint32_t R = (uint32_t)l.R;
+  bool ok = encode_2d(&a.x_map, l.x, dtype, (uint64_t)l.in_dim, (uint64_t)l.S, (uint64_t)l.x_stride, kTcBK, kTcTileM) &&
+            encode_2d(&a.mid_map, l.mid, dtype, (uint64_t)l.n_mod * R, (uint64_t)l.S, (uint64_t)l.mid_stride, R,
+                      kTcTileM);
   for (int m = 0; m < l.n_mod && ok; ++m) {
     a.mod[m] = l.mod[m];
-    ok = encode_2d(&a.a_map[m], l.mod[m].a, dtype, (uint64_t)l.in_dim, (uint64_t)l.num_slots * l.R, (uint64_t)l.in_dim,
-                   kTcR) &&
-         encode_2d(&a.b_map[m], l.mod[m].b, dtype, (uint64_t)l.R, (uint64_t)l.num_slots * l.mod[m].out_dim,
-                   (uint64_t)l.R, kTcBN) &&
+    ok = encode_2d(&a.a_map[m], l.mod[m].a, dtype, (uint64_t)l.in_dim, (uint64_t)l.num_slots * R, (uint64_t)l.in_dim,
+                   kTcBK, R) &&
+         encode_2d(&a.b_map[m], l.mod[m].b, dtype, R, (uint64_t)l.num_slots * l.mod[m].out_dim, R, R, kTcBN) &&
          encode_2d(&a.y_map[m], l.mod[m].y, dtype, (uint64_t)l.mod[m].out_dim, (uint64_t)l.S,
-                   (uint64_t)l.mod[m].y_stride, kTcTileM);
+                   (uint64_t)l.mod[m].y_stride, kTcBK, kTcTileM);
   }
   if (!ok) return cudaErrorNotSupported;
-  return dtype == kBF16 ? launch_prefill_t<__nv_bfloat16>(a, dtype, st, pdl) : launch_prefill_t<__half>(a, dtype, st, pdl);
+  return dtype == kBF16 ? launch_prefill_r<__nv_bfloat16>(a, st, pdl) : launch_prefill_r<__half>(a, st, pdl);
 }
 
 }  // namespace mlora

@@ -33,15 +33,19 @@ __device__ __forceinline__ void tma_prefetch_map(const CUtensorMap* map) {
 
 // ---- UMMA descriptors ---------------------------------------------------------
 
-// Shared-memory matrix descriptor: K-major, SWIZZLE_128B, 8-row groups 1024 B
-// apart (rows of 128 B packed). Advance by 32 B (one K=16 step) with `+ 2`.
-__device__ __forceinline__ uint64_t umma_desc_sw128(const void* tile) {
+// Shared-memory matrix descriptor of a K-major tile whose rows are `row_bytes`
+// (32, 64 or 128) long and swizzled with the same span (SWIZZLE_32B / 64B /
+// 128B: the layout a TMA load with that swizzle writes), 8-row groups packed
+// (stride byte offset 8 * row_bytes). Advance by 32 B (one K=16 step) with `+ 2`.
+__device__ __forceinline__ uint64_t umma_desc_kmajor(const void* tile, int row_bytes) {
   const uint64_t a = (uint64_t)((smem_addr(tile) >> 4) & 0x3FFFu);
-  return a | (1ull << 16)      // leading byte offset (unused for swizzled K-major)
-         | (64ull << 32)       // stride byte offset: 1024 B between 8-row groups
-         | (1ull << 46)        // descriptor version (sm_100)
-         | (2ull << 61);       // layout: SWIZZLE_128B
+  const uint64_t layout = row_bytes == 128 ? 2ull : row_bytes == 64 ? 4ull : 6ull;
+  return a | (1ull << 16)                        // leading byte offset (unused for swizzled K-major)
+         | ((uint64_t)(row_bytes / 2) << 32)     // stride byte offset: 8 rows, in 16-byte units
+         | (1ull << 46)                          // descriptor version (sm_100)
+         | (layout << 61);                       // layout: SWIZZLE_128B / 64B / 32B
 }
+__device__ __forceinline__ uint64_t umma_desc_sw128(const void* tile) { return umma_desc_kmajor(tile, 128); }
 
 // Instruction descriptor of tcgen05.mma.kind::f16: fp32 accumulate, A and B of
 // the same 16-bit type (bf16 when `bf16`), both K-major, shape M x N.
@@ -104,9 +108,13 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Byte offset of element (row, col) in a 128-byte-swizzled tile of 64-column rows.
-__device__ __forceinline__ uint32_t sw128_offset(int row, int col) {
-  return (uint32_t)row * 128u + ((uint32_t)(((col >> 3) ^ (row & 7)) << 4)) + (uint32_t)(col & 7) * 2u;
+// Byte offset of 16-bit element (row, col) in a tile of `row_bytes`-long rows
+// swizzled with the same span (16-byte chunk index XOR-ed with address bits
+// 7.. of the row start; the tile base is aligned to 8 rows).
+__device__ __forceinline__ uint32_t sw_offset(int row, int col, int row_bytes) {
+  const int sel = row_bytes == 128 ? (row & 7) : row_bytes == 64 ? ((row >> 1) & 3) : ((row >> 2) & 1);
+  return (uint32_t)row * (uint32_t)row_bytes + ((uint32_t)(((col >> 3) ^ sel) << 4)) + (uint32_t)(col & 7) * 2u;
 }
+__device__ __forceinline__ uint32_t sw128_offset(int row, int col) { return sw_offset(row, col, 128); }
 
 }  // namespace mlora

@@ -248,6 +248,9 @@ TC_SHAPES = [
     (1024, 1000, 64, [64, 8, 33, 0], [200, 150, 77, 90]),      # ranks < R (NaN-planted tails), base segment,
                                                                # out % 128 != 0 (partial column block)
     (4096, 1024, 64, [64] * 8, [469, 845, 454, 989, 348, 314, 495, 426]),  # cfg3 k/v projection, full size
+    (512, 384, 16, [16, 16, 8], [300, 129, 64]),               # max_rank 16: 32-byte swizzled rank tiles
+    (1024, 1000, 32, [32, 8, 17, 0], [200, 150, 77, 90]),      # max_rank 32: 64-byte swizzle, odd rank 17
+    (4096, 4096, 16, [16] * 8, [469, 845, 454, 989, 348, 314, 495, 426]),  # cfg3 q shape at rank 16
 ]
 
 
@@ -260,13 +263,14 @@ def test_tc_apply_matches_oracle(cuda_dev, dtype, shape):
     _check_apply(c, cuda_dev, dtype, expect_path=4)
 
 
-def test_tc_group_matches_separate_projections(cuda_dev):
+@pytest.mark.parametrize("R, ranks", [(64, [64, 8, 33]), (16, [16, 8, 13]), (32, [32, 32, 24])])
+def test_tc_group_matches_separate_projections(cuda_dev, R, ranks):
     """q/k/v-like group on the tensor-core pair: mid [S, 3R] holds one column block per projection."""
     import ctypes
 
     dev, dt = cuda_dev, torch.bfloat16
-    g = torch.Generator().manual_seed(77)
-    outs, R, ranks, lens, n_in = (512, 256, 128), 64, [64, 8, 33], [150, 90, 70], 640
+    g = torch.Generator().manual_seed(77 + R)
+    outs, lens, n_in = (512, 256, 128), [150, 90, 70], 640
     K, S = len(ranks), sum(lens)
     widx = [0, 1, 2]
     scal = [0.5 + i for i in range(K)]
