@@ -8,9 +8,10 @@
 // for up to four projections that share x and the routing.
 //
 // Work decomposition. Every CTA rebuilds the batch's slot -> token lists from
-// the routing tables in shared memory (a counting sort; slots of rank 0 or
-// with no tokens drop out) and cuts each slot's tokens into tiles of up to
-// kStreamTM rows. Items are then dealt round-robin to one CTA per SM:
+// the routing tables in shared memory (a counting sort, stable in segment
+// order so that every CTA cuts the same tiles; slots of rank 0 or with no
+// tokens drop out) and cuts each slot's tokens into tiles of up to kStreamTM
+// rows. Items are then dealt round-robin to one CTA per SM:
 //   shrink kernel: item = (tile, projection); it streams A[slot, :rank, :] and
 //     the tile's x rows through the shared-memory ring in chunks of KC input
 //     columns and accumulates mid for the tile over the whole input dim, so
@@ -75,7 +76,7 @@ struct ExpandStage {
 // Routing arrays in dynamic shared memory behind the ring.
 struct StreamRouting {
   int* cnt;     // [num_slots] tokens routed to the slot (0 if unused or rank 0)
-  int* fill;    // [num_slots] counting-sort cursor
+  int* fill;    // [num_slots] rows placed so far
   int* off;     // [num_slots] first entry of the slot in tok
   int* toff;    // [num_slots + 1] first tile of the slot; toff[num_slots] = tiles
   int* rank;    // [num_slots] rank clamped to [0, R]
@@ -100,7 +101,7 @@ __device__ __forceinline__ StreamRouting stream_routing(unsigned char* base, int
   return r;
 }
 
-// Counting sort of the batch's tokens by slot (every thread of the CTA).
+// Counting sort of the batch's tokens by slot, stable in segment order.
 // Reads only routing tables and ranks/scalings, which no kernel of the step writes.
 __device__ void stream_build_routing(const StreamArgs& p, const StreamRouting& rt, bool want_scale) {
   __shared__ int s_overflow;
@@ -173,11 +174,38 @@ __device__ void stream_build_routing(const StreamArgs& p, const StreamRouting& r
   }
   __syncthreads();
   if (s_overflow) return;
-  for (int i = tid; i < p.bs; i += nt) {
-    const int w = __ldg(p.weight_indices + i);
-    const int st = __ldg(p.seg_indptr + i), en = __ldg(p.seg_indptr + i + 1);
-    if (w < 0 || w >= p.num_slots || st < 0 || en < st || en > p.S || rt.rank[w] == 0) continue;
-    for (int row = st; row < en; ++row) rt.tok[rt.off[w] + atomicAdd(&rt.fill[w], 1)] = row;
+  // Token lists in segment order, identical in every CTA (tiles of a slot are
+  // cut from this order, and different CTAs must agree on them): warp 0 walks
+  // the segments 32 at a time; lanes of one slot (match_any) place their rows
+  // after the slot's earlier segments.
+  if (tid < 32) {
+    const int lane = tid;
+    for (int s0 = 0; s0 < p.bs; s0 += 32) {
+      const int i = s0 + lane;
+      int w = -1, st = 0, en = 0;
+      if (i < p.bs) {
+        w = __ldg(p.weight_indices + i);
+        st = __ldg(p.seg_indptr + i);
+        en = __ldg(p.seg_indptr + i + 1);
+        if (w < 0 || w >= p.num_slots || st < 0 || en < st || en > p.S || rt.rank[w] == 0) w = -1;
+      }
+      const int len = w >= 0 ? en - st : 0;
+      const unsigned peers = __match_any_sync(0xffffffffu, w >= 0 ? w : -1 - lane);
+      const unsigned lower = peers & ((1u << lane) - 1u);
+      int pre = 0;  // rows of this slot's segments on lower lanes
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        const int v = __shfl_sync(0xffffffffu, len, k);
+        if ((lower >> k) & 1u) pre += v;
+      }
+      const int base = w >= 0 ? rt.fill[w] : 0;
+      __syncwarp();
+      if (w >= 0) {
+        for (int row = st; row < en; ++row) rt.tok[rt.off[w] + base + pre + (row - st)] = row;
+        if (lane == 31 - __clz(peers)) rt.fill[w] = base + pre + len;  // the slot's last lane in this pass
+      }
+      __syncwarp();
+    }
   }
   __syncthreads();
 }

@@ -318,6 +318,44 @@ def test_stream_apply_many_slots_and_long_segments(cuda_dev):
     _check_apply(c, cuda_dev, torch.bfloat16, expect_path=3, force="stream")
 
 
+@pytest.mark.parametrize("n_slots", [8, 32])
+def test_stream_apply_many_one_token_segments_per_slot(cuda_dev, n_slots):
+    """Hundreds of one-token segments over few slots: each slot spans several
+    tiles, and every CTA must cut them identically (a single apply and a group)."""
+    dev = cuda_dev
+    c = _case(40 + n_slots, torch.bfloat16, 1024, 1024, 16, [16] * n_slots, [1] * 256, dev)
+    _check_apply(c, dev, torch.bfloat16, expect_path=3)  # 256 rows: the automatic choice
+    import ctypes
+
+    g = torch.Generator().manual_seed(n_slots)
+    outs = (1024, 256, 256)
+    x = torch.randn(256, 1024, generator=g).bfloat16()
+    widx = torch.randint(0, n_slots, (256,), generator=g).tolist()
+    ranks, scal = [16] * n_slots, [2.0] * n_slots
+    meta = C.make_meta([1] * 256, widx, ranks, scal, dev)
+    As = [((torch.rand(n_slots, 16, 1024, generator=g) * 2 - 1) / 32).bfloat16() for _ in outs]
+    Bs = [(torch.randn(n_slots, o, 16, generator=g) * 0.02).bfloat16() for o in outs]
+    y0 = [torch.randn(256, o, generator=g).bfloat16() for o in outs]
+    ys = [y.to(dev).clone() for y in y0]
+    xd, Ad, Bd = x.to(dev), [a.to(dev) for a in As], [b.to(dev) for b in Bs]  # alive across the launch
+    mid = torch.zeros(256, 64, dtype=torch.bfloat16, device=dev)
+    P = ctypes.c_void_p
+    arr = lambda vals, t: (t * 3)(*vals)  # noqa: E731
+    m = meta.struct()
+    rc = _native.capi().mlora_apply_lora_group(
+        xd.data_ptr(), 256, 1024, 1024, 3, arr([a.data_ptr() for a in Ad], P),
+        arr([b.data_ptr() for b in Bd], P), arr(list(outs), ctypes.c_int64), arr([y.data_ptr() for y in ys], P),
+        arr([y.stride(0) for y in ys], ctypes.c_int64), 16, ctypes.byref(m), mid.data_ptr(), 64, 0, None,
+        torch.cuda.current_stream().cuda_stream)
+    C.check(rc)
+    assert _native.capi().mlora_last_apply_path() == 3
+    torch.cuda.synchronize()
+    ind = meta.seg_indptr.cpu().numpy()
+    for a, b, yb, y in zip(As, Bs, y0, ys):
+        want = O.apply_lora_fp32(C.f32(x), C.f32(a), C.f32(b), ind, widx, ranks, scal, 256, C.f32(yb))
+        np.testing.assert_allclose(C.f32(y), want, rtol=RTOL, atol=ATOL)
+
+
 def test_stream_apply_is_deterministic(cuda_dev):
     """Two calls in a row on the same inputs give bit-identical y and mid."""
     c = _case(33, torch.bfloat16, 4096, 4096, 16, [16] * 32, [1] * 64, cuda_dev, nan_tails=False)
