@@ -373,6 +373,20 @@ CFG4_RANKS = (8, 16, 32, 64)
 CFG4_TEMPLATES = 8  # distinct host weight sets per rank (adapters share them; every load still copies its bank)
 
 
+def admit(queue: list, slots: int):
+    """cfg4 admission: tokens in queue order join the batch while their adapter
+    is already admitted or fewer than ``slots`` adapters are; the others are
+    deferred (returned in order) to the next step."""
+    admitted, deferred, distinct = [], [], set()
+    for name in queue:
+        if name in distinct or len(distinct) < slots:
+            distinct.add(name)
+            admitted.append(name)
+        else:
+            deferred.append(name)
+    return admitted, deferred, distinct
+
+
 def module_keys(layers: int):
     proj = {"q": "self_attn.q_proj", "k": "self_attn.k_proj", "v": "self_attn.v_proj", "o": "self_attn.o_proj",
             "gate": "mlp.gate_proj", "up": "mlp.up_proj", "down": "mlp.down_proj"}
@@ -448,15 +462,7 @@ def run_pool_workload(args, wl: Workload, dev) -> None:
     def next_batch():
         nonlocal pending
         draws = list(rng.choice(wl.adapters, size=T - len(pending), p=p_zipf))
-        queue = pending + [f"a{int(i)}" for i in draws]
-        admitted, keep, distinct = [], [], set()
-        for nm in queue:
-            if nm in distinct or len(distinct) < POOL_SLOTS:
-                distinct.add(nm)
-                admitted.append(nm)
-            else:
-                keep.append(nm)
-        pending = keep
+        admitted, pending, distinct = admit(pending + [f"a{int(i)}" for i in draws], POOL_SLOTS)
         return admitted, distinct
 
     be = CudaLoRABackend()
