@@ -23,7 +23,7 @@
 // One producer warp fills a kStreamStages-deep shared-memory ring with 1-D
 // TMA bulk copies (lane 0 arms the stage's full mbarrier with the byte count,
 // the lanes issue one row copy each: a single issuing thread was measured at
-// ~75-100 ns per bulk copy, too slow for row-sized pieces); four consumer
+// ~75-100 ns per bulk copy, too slow for row-sized pieces); eight consumer
 // warps run mma.sync m16n8k16 tiles and release stages on empty mbarriers.
 // The weights of the first ring fills are requested BEFORE griddepcontrol.wait,
 // so under programmatic dependent launch they stream while the previous
@@ -42,7 +42,7 @@
 
 namespace mlora {
 
-constexpr int kStreamConsumers = 4;                          // consumer warps
+constexpr int kStreamConsumers = 8;                          // consumer warps
 constexpr int kStreamThreads = (kStreamConsumers + 1) * 32;  // + one producer warp
 constexpr int kStreamTM = 8;                                 // tokens per tile
 constexpr int kStreamStages = 4;
