@@ -371,8 +371,8 @@ __global__ void __launch_bounds__(kFusedNT) apply_fused_kernel(const FusedArgs p
         const int brow = lane & 7, bhalf = (lane >> 3) & 1;
         const int ntiles = (olen + 7) / 8;
         const int ksteps_r = (rank + 15) / 16;
-        for (int nb = warp; nb < ntiles; nb += NW) {
-          float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        auto tile_mma = [&](int nb, float (&acc)[4]) {
+          acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
 #pragma unroll
           for (int kk = 0; kk < RM / 16; ++kk) {
             if (kk < ksteps_r) {
@@ -385,23 +385,31 @@ __global__ void __launch_bounds__(kFusedNT) apply_fused_kernel(const FusedArgs p
               mma_16816<T>(acc, am[kk][0], am[kk][1], am[kk][2], am[kk][3], b0, b1);
             }
           }
+        };
+        auto tile_store = [&](int nb, const float (&acc)[4]) {
           if (g < nt) {  // row g of the tile: outputs o, o + 1
             const int ol = nb * 8 + 2 * cq;
             const int o = o_lo + ol;
             T* yp = ybase + (int64_t)s_rows[g] * m.y_stride + o;
             if (o + 1 < o_hi && m.y_tma) {
-              const T* ys = s_y + (size_t)g * p.ob_max + ol;
-              T v[2];
-              v[0] = Num<T>::from_f(round_to<T>(acc[0] * scale) + Num<T>::to_f(ys[0]));
-              v[1] = Num<T>::from_f(round_to<T>(acc[1] * scale) + Num<T>::to_f(ys[1]));
-              uint32_t u;
-              memcpy(&u, v, 4);
-              *reinterpret_cast<uint32_t*>(yp) = u;
+              const uint32_t u = *reinterpret_cast<const uint32_t*>(s_y + (size_t)g * p.ob_max + ol);
+              *reinterpret_cast<uint32_t*>(yp) =
+                  Pack2<T>::pack(Num<T>::from_f(round_to<T>(acc[0] * scale) + Pack2<T>::lo(u)),
+                                 Num<T>::from_f(round_to<T>(acc[1] * scale) + Pack2<T>::hi(u)));
             } else {
               if (o < o_hi) yp[0] = Num<T>::from_f(round_to<T>(acc[0] * scale) + ldcg_f<T>(yp));
               if (o + 1 < o_hi) yp[1] = Num<T>::from_f(round_to<T>(acc[1] * scale) + ldcg_f<T>(yp + 1));
             }
           }
+        };
+        // two output tiles per iteration: independent tensor-core chains overlap their latencies
+        for (int nb = warp; nb < ntiles; nb += 2 * NW) {
+          float acc0[4], acc1[4];
+          const bool two = nb + NW < ntiles;
+          tile_mma(nb, acc0);
+          if (two) tile_mma(nb + NW, acc1);
+          tile_store(nb, acc0);
+          if (two) tile_store(nb + NW, acc1);
         }
       }
       const bool more = (q0 + TT < ntok) || (from + kFusedScan < p.bs);

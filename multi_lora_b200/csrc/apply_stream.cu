@@ -499,8 +499,8 @@ __global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(cons
       const int ksteps = (rank + 15) / 16;
       const uint32_t ba = smem_addr(stage_b(s));
       T* ys = stage_y(s);
-      for (int nb = warp; nb < it.ocl / 8; nb += NC) {
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      auto tile_mma = [&](int nb, float (&acc)[4]) {
+        acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
 #pragma unroll
         for (int kk = 0; kk < RM / 16; ++kk) {
           if (kk < ksteps) {
@@ -513,12 +513,23 @@ __global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(cons
             mma_16816<T>(acc, am[kk][0], am[kk][1], am[kk][2], am[kk][3], b0, b1);
           }
         }
-        if (g < nt) {
+      };
+      auto tile_store = [&](int nb, const float (&acc)[4]) {
+        if (g < nt) {  // y = T(T(scale * acc) + y), in place in the staged tile
           uint32_t* yp = reinterpret_cast<uint32_t*>(ys + g * OCP + nb * 8 + 2 * cq);
           const uint32_t u = *yp;
           *yp = Pack2<T>::pack(Num<T>::from_f(round_to<T>(acc[0] * scale) + Pack2<T>::lo(u)),
                                Num<T>::from_f(round_to<T>(acc[1] * scale) + Pack2<T>::hi(u)));
         }
+      };
+      // two output tiles per iteration: independent tensor-core chains overlap their latencies
+      for (int nb = warp; nb < it.ocl / 8; nb += 2 * NC) {
+        float acc0[4], acc1[4];
+        const bool two = nb + NC < it.ocl / 8;
+        tile_mma(nb, acc0);
+        if (two) tile_mma(nb + NC, acc1);
+        tile_store(nb, acc0);
+        if (two) tile_store(nb + NC, acc1);
       }
     }
     fence_proxy_async_smem();  // the y tile written above is read next by the bulk stores
