@@ -45,7 +45,8 @@ namespace mlora {
 constexpr int kStreamConsumers = 8;                          // consumer warps
 constexpr int kStreamThreads = (kStreamConsumers + 1) * 32;  // + one producer warp
 constexpr int kStreamTM = 8;                                 // tokens per tile
-constexpr int kStreamStages = 4;
+constexpr int kStreamStages = 4;        // expand ring
+constexpr int kStreamShrinkStages = 2;  // shrink ring (stages twice as wide: half the row copies per byte)
 
 // Input columns per shrink chunk and B rows per expand block: ~16 KB of
 // weights per ring stage at every rank.
@@ -55,7 +56,7 @@ __host__ __device__ constexpr int align128(int b) { return (b + 127) / 128 * 128
 
 template <int RM>
 struct ShrinkStage {
-  static constexpr int KC = stream_kc(RM);
+  static constexpr int KC = 2 * stream_kc(RM);
   static constexpr int KCP = KC + 8;  // padded row (odd number of 16-byte units: ldmatrix conflict-free)
   static constexpr int A_BYTES = align128(RM * KCP * 2);
   static constexpr int X_BYTES = align128(kStreamTM * KCP * 2);
@@ -247,7 +248,7 @@ __device__ __forceinline__ StreamModule stream_module(const StreamArgs& p, int m
 template <typename T, int RM>
 __global__ void __launch_bounds__(kStreamThreads) lora_shrink_stream_kernel(const StreamArgs p) {
   using SS = ShrinkStage<RM>;
-  constexpr int NC = kStreamConsumers, NS = kStreamStages, TM = kStreamTM;
+  constexpr int NC = kStreamConsumers, NS = kStreamShrinkStages, TM = kStreamTM;
   constexpr int KC = SS::KC, KCP = SS::KCP;
   extern __shared__ __align__(128) unsigned char s_dyn[];
   __shared__ __align__(8) uint64_t full[NS], empty[NS];
@@ -584,7 +585,7 @@ cudaError_t launch_stream_rm(const StreamArgs& a, cudaStream_t st, bool pdl) {
   static std::mutex mu;
   static int set_s = 0, set_e = 0;
   const int route = align128(stream_routing_bytes(a.num_slots, a.S));
-  const int smem_s = kStreamStages * ShrinkStage<RM>::BYTES + route;
+  const int smem_s = kStreamShrinkStages * ShrinkStage<RM>::BYTES + route;
   const int smem_e = kStreamStages * ExpandStage<RM>::BYTES + route;
   auto ks = lora_shrink_stream_kernel<T, RM>;
   auto ke = lora_expand_stream_kernel<T, RM>;
