@@ -45,7 +45,7 @@ namespace mlora {
 constexpr int kStreamConsumers = 8;                          // consumer warps
 constexpr int kStreamThreads = (kStreamConsumers + 1) * 32;  // + one producer warp
 constexpr int kStreamTM = 8;                                 // tokens per tile
-constexpr int kStreamStages = 4;        // expand ring
+constexpr int kStreamStages = 2;        // expand ring
 constexpr int kStreamShrinkStages = 2;  // shrink ring (stages twice as wide: half the row copies per byte)
 
 // Input columns per shrink chunk and B rows per expand block: ~16 KB of
@@ -65,7 +65,7 @@ struct ShrinkStage {
 
 template <int RM>
 struct ExpandStage {
-  static constexpr int OC = stream_kc(RM);
+  static constexpr int OC = 2 * stream_kc(RM);
   static constexpr int OCP = OC + 8;
   static constexpr int MP = RM + 8;
   static constexpr int B_BYTES = align128(OC * RM * 2 + 16);  // + slack: a half k-step may read 16 B past the block
