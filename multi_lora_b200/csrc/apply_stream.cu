@@ -47,6 +47,7 @@ constexpr int kStreamThreads = (kStreamConsumers + 1) * 32;  // + one producer w
 constexpr int kStreamTM = 8;                                 // tokens per tile
 constexpr int kStreamStages = 2;        // expand ring
 constexpr int kStreamShrinkStages = 2;  // shrink ring (stages twice as wide: half the row copies per byte)
+constexpr int kStreamShrinkSplit = 4;   // CTAs per shrink item (a cluster splitting the input dim)
 
 // Input columns per shrink chunk and B rows per expand block: ~16 KB of
 // weights per ring stage at every rank.
@@ -248,19 +249,23 @@ __device__ __forceinline__ StreamModule stream_module(const StreamArgs& p, int m
 template <typename T, int RM>
 __global__ void __launch_bounds__(kStreamThreads) lora_shrink_stream_kernel(const StreamArgs p) {
   using SS = ShrinkStage<RM>;
-  constexpr int NC = kStreamConsumers, NS = kStreamShrinkStages, TM = kStreamTM;
+  constexpr int NC = kStreamConsumers, NS = kStreamShrinkStages, TM = kStreamTM, KS = kStreamShrinkSplit;
   constexpr int KC = SS::KC, KCP = SS::KCP;
+  constexpr uint32_t PB = TM * RM * 4;  // one CTA's fp32 partial tile
   extern __shared__ __align__(128) unsigned char s_dyn[];
-  __shared__ __align__(8) uint64_t full[NS], empty[NS];
+  __shared__ __align__(8) uint64_t full[NS], empty[NS], bar_red[2], bar_free[2];
   __shared__ __align__(16) float s_red[NC][TM][RM];
+  __shared__ __align__(16) float s_recv[2][KS][TM][RM];  // used in cluster rank 0
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const StreamRouting rt = stream_routing(s_dyn + NS * SS::BYTES, p.num_slots);
   stream_build_routing(p, rt, false);
   const int tiles = rt.toff[p.num_slots];
   const int n_items = tiles * p.n_mod;
-  const int G = gridDim.x;
-  const int my_items = blockIdx.x < n_items ? (n_items - 1 - blockIdx.x) / G + 1 : 0;
+  // one thread-block cluster of KS CTAs per item: CTA `crank` streams its share
+  // of the input dim; the partial tiles meet in CTA 0 (distributed shared memory)
+  const int crank = (int)(blockIdx.x % KS), cl = (int)(blockIdx.x / KS), NCL = (int)(gridDim.x / KS);
+  const int my_items = cl < n_items ? (n_items - 1 - cl) / NCL + 1 : 0;  // the same for the whole cluster
   if (my_items == 0) {
     pdl_trigger();
     return;
@@ -270,20 +275,27 @@ __global__ void __launch_bounds__(kStreamThreads) lora_shrink_stream_kernel(cons
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], NC);
     }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bar_red[s], 1);
+      mbar_init(&bar_free[s], 1);
+    }
     fence_barrier_init();
   }
   __syncthreads();
-  pdl_trigger();  // the expand kernel may launch now and prefetch its weights
+  cluster_arrive_release();
+  cluster_wait_acquire();  // every CTA's barriers exist before any remote operation
+  pdl_trigger();           // the expand kernel may launch now and prefetch its weights
 
   const int nch = (p.in_dim + KC - 1) / KC;
-  const int total = my_items * nch;  // ring fills of this CTA
+  const int c_lo = crank * nch / KS, cnt = (crank + 1) * nch / KS - c_lo;  // this CTA's chunks per item
+  const int total = my_items * cnt;                                         // ring fills of this CTA
   if (warp == NC) {
     // ---------------- producer warp: lane 0 arms the stage, every lane issues copies ----------------
     auto stage_a = [&](int s) { return reinterpret_cast<T*>(s_dyn + s * SS::BYTES); };
     auto stage_x = [&](int s) { return reinterpret_cast<T*>(s_dyn + s * SS::BYTES + SS::A_BYTES); };
     auto issue_a = [&](int f) {
       const int s = f % NS;
-      const int item = blockIdx.x + (f / nch) * G, c = f % nch;
+      const int item = cl + (f / cnt) * NCL, c = c_lo + f % cnt;
       const StreamTile t = stream_tile(rt, p.num_slots, item / p.n_mod);
       const int k0 = c * KC, kcl = min(KC, p.in_dim - k0);
       if (lane == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(t.rank + t.nt) * kcl * sizeof(T));
@@ -294,7 +306,7 @@ __global__ void __launch_bounds__(kStreamThreads) lora_shrink_stream_kernel(cons
     };
     auto issue_x = [&](int f) {
       const int s = f % NS;
-      const int item = blockIdx.x + (f / nch) * G, c = f % nch;
+      const int item = cl + (f / cnt) * NCL, c = c_lo + f % cnt;
       const StreamTile t = stream_tile(rt, p.num_slots, item / p.n_mod);
       const int k0 = c * KC, kcl = min(KC, p.in_dim - k0);
       const T* x = static_cast<const T*>(p.x) + k0;
@@ -311,65 +323,100 @@ __global__ void __launch_bounds__(kStreamThreads) lora_shrink_stream_kernel(cons
       issue_a(f);
       issue_x(f);
     }
-    return;
-  }
-
-  // ---------------- consumers ----------------
-  const int ctid = tid;  // 0 .. NC*32-1
-  const int g = lane >> 2, cq = lane & 3;
-  bool ok = true;
-  int f = 0;
-  for (int j = 0; j < my_items; ++j) {
-    const int item = blockIdx.x + j * G;
-    const int m = item % p.n_mod;
-    const StreamTile t = stream_tile(rt, p.num_slots, item / p.n_mod);
-    float acc[RM / 8][4];
+  } else {
+    // ---------------- consumers ----------------
+    const int ctid = tid;  // 0 .. NC*32-1
+    const int g = lane >> 2, cq = lane & 3;
+    bool ok = true;
+    int f = 0;
+    const uint32_t recv0 = smem_addr(&s_recv[0][0][0][0]);
+    for (int j = 0; j < my_items; ++j) {
+      const int item = cl + j * NCL;
+      const int m = item % p.n_mod;
+      const int par = j & 1;
+      const StreamTile t = stream_tile(rt, p.num_slots, item / p.n_mod);
+      float acc[RM / 8][4];
 #pragma unroll
-    for (int i = 0; i < RM / 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-    const int xrow = (lane & 15) < t.nt ? (lane & 15) : 0;  // MMA rows past the tile repeat row 0
-    const int brow = lane & 7, bhalf = (lane >> 3) & 1;
-    for (int c = 0; c < nch; ++c, ++f) {
-      const int s = f % NS;
-      if (ok) ok = mbar_wait(&full[s], (f / NS) & 1, p.status);  // after a timeout: no more waits
-      if (ok) {
-        const int ksteps = min(KC, p.in_dim - c * KC) / 16;
-        const uint32_t xa = smem_addr(s_dyn + s * SS::BYTES + SS::A_BYTES) + (uint32_t)(xrow * KCP + (lane >> 4) * 8) * 2u;
-        const uint32_t aa = smem_addr(s_dyn + s * SS::BYTES);
-        for (int kk = warp; kk < ksteps; kk += NC) {
-          uint32_t a0, a1, a2, a3;
-          ldsm_x4(xa + (uint32_t)kk * 32u, a0, a1, a2, a3);
+      for (int i = 0; i < RM / 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+      const int xrow = (lane & 15) < t.nt ? (lane & 15) : 0;  // MMA rows past the tile repeat row 0
+      const int brow = lane & 7, bhalf = (lane >> 3) & 1;
+      for (int c = 0; c < cnt; ++c, ++f) {
+        const int s = f % NS;
+        if (ok) ok = mbar_wait(&full[s], (f / NS) & 1, p.status);  // after a timeout: no more waits
+        if (ok) {
+          const int ksteps = min(KC, p.in_dim - (c_lo + c) * KC) / 16;
+          const uint32_t xa = smem_addr(s_dyn + s * SS::BYTES + SS::A_BYTES) + (uint32_t)(xrow * KCP + (lane >> 4) * 8) * 2u;
+          const uint32_t aa = smem_addr(s_dyn + s * SS::BYTES);
+          for (int kk = warp; kk < ksteps; kk += NC) {
+            uint32_t a0, a1, a2, a3;
+            ldsm_x4(xa + (uint32_t)kk * 32u, a0, a1, a2, a3);
 #pragma unroll
-          for (int i = 0; i < RM / 8; ++i) {
-            if (i * 8 < t.rank) {
-              uint32_t b0, b1;
-              ldsm_x2(aa + (uint32_t)((i * 8 + brow) * KCP + kk * 16 + bhalf * 8) * 2u, b0, b1);
-              mma_16816<T>(acc[i], a0, a1, a2, a3, b0, b1);
+            for (int i = 0; i < RM / 8; ++i) {
+              if (i * 8 < t.rank) {
+                uint32_t b0, b1;
+                ldsm_x2(aa + (uint32_t)((i * 8 + brow) * KCP + kk * 16 + bhalf * 8) * 2u, b0, b1);
+                mma_16816<T>(acc[i], a0, a1, a2, a3, b0, b1);
+              }
             }
           }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
-    }
-    // cross-warp reduction in warp order, one rounding to T, rows of this tile only
+      // this CTA's partial: the warps' tiles summed in warp order ...
 #pragma unroll
-    for (int i = 0; i < RM / 8; ++i) {
-      s_red[warp][g][i * 8 + 2 * cq] = acc[i][0];
-      s_red[warp][g][i * 8 + 2 * cq + 1] = acc[i][1];
-    }
-    named_barrier(1, NC * 32);
-    if (ok) {
-      T* mid = static_cast<T*>(p.mid) + m * p.R;
-      for (int e = ctid; e < t.nt * t.rank; e += NC * 32) {
-        const int r = e / t.rank, k = e - r * t.rank;
-        float v = 0.f;
+      for (int i = 0; i < RM / 8; ++i) {
+        s_red[warp][g][i * 8 + 2 * cq] = acc[i][0];
+        s_red[warp][g][i * 8 + 2 * cq + 1] = acc[i][1];
+      }
+      named_barrier(1, NC * 32);
+      // ... pushed into slot `crank` of CTA 0's receive buffer (once CTA 0 has
+      // released that buffer from item j - 2)
+      if (j >= 2 && crank != 0 && ok) ok = mbar_wait(&bar_free[par], ((j >> 1) - 1) & 1, p.status);
+      {
+        const uint32_t dst = cluster_map(recv0 + (uint32_t)((par * KS + crank) * TM * RM) * 4u, 0);
+        const uint32_t bar = cluster_map(smem_addr(&bar_red[par]), 0);
+        for (int e = ctid; e < TM * RM / 4; e += NC * 32) {
+          const int r = e / (RM / 4), c4 = (e % (RM / 4)) * 4;
+          float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-        for (int w = 0; w < NC; ++w) v += s_red[w][r][k];
-        mid[(int64_t)rt.tok[t.start + r] * p.mid_stride + k] = Num<T>::from_f(v);
+          for (int w = 0; w < NC; ++w) {
+            const float4 u = *reinterpret_cast<const float4*>(&s_red[w][r][c4]);
+            v.x += u.x;
+            v.y += u.y;
+            v.z += u.z;
+            v.w += u.w;
+          }
+          st_async_v4(dst + (uint32_t)(r * RM + c4) * 4u, v.x, v.y, v.z, v.w, bar);
+        }
+      }
+      named_barrier(1, NC * 32);  // s_red may be overwritten by the next item
+      if (crank == 0) {
+        // CTA 0: the KS partials in cluster order, one rounding to T, rows of this tile only
+        if (ctid == 0) mbar_arrive_expect_tx(&bar_red[par], (uint32_t)KS * PB);
+        if (ok) ok = mbar_wait(&bar_red[par], (j >> 1) & 1, p.status);
+        if (ok) {
+          T* mid = static_cast<T*>(p.mid) + m * p.R;
+          for (int e = ctid; e < t.nt * t.rank; e += NC * 32) {
+            const int r = e / t.rank, k = e - r * t.rank;
+            float v = 0.f;
+#pragma unroll
+            for (int q = 0; q < KS; ++q) v += s_recv[par][q][r][k];
+            mid[(int64_t)rt.tok[t.start + r] * p.mid_stride + k] = Num<T>::from_f(v);
+          }
+        }
+        named_barrier(1, NC * 32);  // done reading s_recv[par]
+        if (ctid > 0 && ctid < KS) {  // release the buffer to the peers for item j + 2
+          asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
+                           cluster_map(smem_addr(&bar_free[par]), (uint32_t)ctid))
+                       : "memory");
+        }
       }
     }
-    named_barrier(1, NC * 32);
   }
+  // no CTA leaves while a peer may still write into its shared memory
+  cluster_arrive_release();
+  cluster_wait_acquire();
 }
 
 // ---------------------------------------------------------------------------
@@ -591,7 +638,21 @@ cudaError_t launch_stream_rm(const StreamArgs& a, cudaStream_t st, bool pdl) {
   auto ke = lora_expand_stream_kernel<T, RM>;
   if (!ensure_smem(ks, smem_s, set_s, mu) || !ensure_smem(ke, smem_e, set_e, mu)) return cudaErrorNotSupported;
   const dim3 grid(stream_sm_count());
-  cudaError_t e = launch_kernel(ks, grid, dim3(kStreamThreads), smem_s, st, pdl, a);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(stream_sm_count() / kStreamShrinkSplit * kStreamShrinkSplit));
+  cfg.blockDim = dim3(kStreamThreads);
+  cfg.dynamicSmemBytes = smem_s;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kStreamShrinkSplit;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, ks, a);
   if (e != cudaSuccess) return e;
   // the expand kernel always follows with the programmatic attribute: its wait is the shrink -> expand edge
   return launch_kernel(ke, grid, dim3(kStreamThreads), smem_e, st, true, a);
