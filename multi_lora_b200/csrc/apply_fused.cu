@@ -62,13 +62,14 @@ __device__ __forceinline__ void fused_scan(FusedSegs& sl, int slot, int from, co
   if (threadIdx.x >= 32) return;
   const int lane = threadIdx.x;
   constexpr int NB = kFusedScan / 32;
+  const int nbv = min(NB, (p.bs - from + 31) / 32);  // batches that hold segments (warp-uniform)
   int w[NB], st[NB], en[NB];
 #pragma unroll
   for (int b = 0; b < NB; ++b) {
     const int idx = from + b * 32 + lane;
     w[b] = -1;
     st[b] = en[b] = 0;
-    if (idx < p.bs) {
+    if (b < nbv && idx < p.bs) {
       w[b] = __ldg(p.weight_indices + idx);
       st[b] = __ldg(p.seg_indptr + idx);
       en[b] = __ldg(p.seg_indptr + idx + 1);
@@ -77,6 +78,7 @@ __device__ __forceinline__ void fused_scan(FusedSegs& sl, int slot, int from, co
   int n = 0, total = 0;
 #pragma unroll
   for (int b = 0; b < NB; ++b) {
+    if (b >= nbv) break;
     const int idx = from + b * 32 + lane;
     bool match = false;
     int len = 0;
@@ -122,13 +124,34 @@ __device__ __forceinline__ int fused_token_row(const FusedSegs& sl, int q) {
   return sl.start[lo] + (q - sl.cum[lo]);
 }
 
+// Walks the flat indices start, start + step, ... of a [rows][cols] space
+// as (r, c) pairs with two divisions in all instead of one per step.
+struct FlatWalk {
+  int r, c, dr, dc, cols;
+  __device__ __forceinline__ FlatWalk(int start, int step, int cols_) : cols(cols_) {
+    r = start / cols;
+    c = start - r * cols;
+    dr = step / cols;
+    dc = step - dr * cols;
+  }
+  __device__ __forceinline__ void next() {
+    r += dr;
+    c += dc;
+    if (c >= cols) {
+      c -= cols;
+      ++r;
+    }
+  }
+};
+
 // Shared-memory row stride (elements) for a row of `k` elements that
 // ldmatrix reads conflict-free: an odd number of 16-byte units.
 __host__ __device__ __forceinline__ int padded_row(int k) { return ((k / 8) % 2 == 0) ? k + 8 : k; }
 
-// RM: rank columns covered by the tiles (16, 32 or 64; >= R).
+// RM: rank columns covered by the tiles (16, 32 or 64; >= R). Register caps
+// at RM 32 / 64 keep 4 / 3 CTAs per SM resident (no spills); RM 16 needs 48.
 template <typename T, int RM>
-__global__ void __launch_bounds__(kFusedNT) apply_fused_kernel(const FusedArgs p) {
+__global__ void __launch_bounds__(kFusedNT, RM == 16 ? 0 : RM == 32 ? 4 : 3) apply_fused_kernel(const FusedArgs p) {
   constexpr int NT = kFusedNT;
   constexpr int NW = NT / 32;
   constexpr int TT = kFusedTT;    // tokens per tile (MMA rows 8..15 repeat row 0 and are discarded)
@@ -219,13 +242,9 @@ __global__ void __launch_bounds__(kFusedNT) apply_fused_kernel(const FusedArgs p
     mbar_arrive_expect_tx(&bar_w, b_bytes);
     if (b_bytes > 0) bulk_copy_g2s(s_b, b_src, b_bytes, &bar_w);
   }
-  {
-    const int kc8 = klen / 8;
-    for (int e = tid; e < rank * kc8; e += NT) {
-      const int n = e / kc8, c = e - n * kc8;
-      cp_async16(s_a + (size_t)n * kp + c * 8, a_src + (int64_t)n * p.in_dim + c * 8);
-    }
-  }
+  if (klen > 0)
+    for (FlatWalk w(tid, NT, klen / 8); w.r < rank; w.next())
+      cp_async16(s_a + (size_t)w.r * kp + w.c * 8, a_src + (int64_t)w.r * p.in_dim + w.c * 8);
   const int rc = (rank + 7) / 8;  // 16-byte B chunks per row that hold rank columns
   if (!b_dense) {  // rows of R with only `rank` valid columns: 16-byte copies per thread
     for (int e = tid; e < olen * rc; e += NT) {
@@ -239,7 +258,7 @@ __global__ void __launch_bounds__(kFusedNT) apply_fused_kernel(const FusedArgs p
 
   const T* __restrict__ xbase = static_cast<const T*>(p.x);
   T* __restrict__ ybase = static_cast<T*>(m.y);
-  const uint32_t sa_addr = smem_addr(s_a), sb_addr = smem_addr(s_b), sx_addr = smem_addr(s_x);
+  const uint32_t sb_addr = smem_addr(s_b);
   const uint32_t smid_addr = smem_addr(&s_mid[0][0]);
   const int g = lane >> 2, cq = lane & 3;
   bool ok = true;
@@ -259,20 +278,18 @@ __global__ void __launch_bounds__(kFusedNT) apply_fused_kernel(const FusedArgs p
         for (int e = tid; e < TT * 8; e += NT) s_x[(size_t)(e / 8) * kp + klen + (e % 8)] = Num<T>::from_f(0.f);
       __syncthreads();
       if (m.y_tma && olen > 0) {  // this tile's y rows (output block), needed only by the expand
-        const int oc8 = olen / 8;
-        for (int e = tid; e < nt * oc8; e += NT) {
-          const int t = e / oc8, c = e - t * oc8;
-          cp_async16(s_y + (size_t)t * p.ob_max + c * 8, ybase + (int64_t)s_rows[t] * m.y_stride + o_lo + c * 8);
-        }
+        for (FlatWalk w(tid, NT, olen / 8); w.r < nt; w.next())
+          cp_async16(s_y + (size_t)w.r * p.ob_max + w.c * 8,
+                     ybase + (int64_t)s_rows[w.r] * m.y_stride + o_lo + w.c * 8);
       }
       cp_async_commit();  // group: this tile's y rows (possibly empty)
       {  // this tile's x rows (k-slice): plain 16-byte loads by every thread (L2 hits)
-        const int kc = klen / 8;
-        for (int e = tid; e < nt * kc; e += NT) {
-          const int t = e / kc, c = e - t * kc;
-          const uint4 v = __ldcg(reinterpret_cast<const uint4*>(xbase + (int64_t)s_rows[t] * p.x_stride + k0) + c);
-          *reinterpret_cast<uint4*>(s_x + (size_t)t * kp + c * 8) = v;
-        }
+        if (klen > 0)
+          for (FlatWalk w(tid, NT, klen / 8); w.r < nt; w.next()) {
+            const uint4 v =
+                __ldcg(reinterpret_cast<const uint4*>(xbase + (int64_t)s_rows[w.r] * p.x_stride + k0) + w.c);
+            *reinterpret_cast<uint4*>(s_x + (size_t)w.r * kp + w.c * 8) = v;
+          }
       }
       if (first) {
         cp_async_wait<1>();  // the weights group (this tile's y group may still be in flight)
@@ -287,35 +304,52 @@ __global__ void __launch_bounds__(kFusedNT) apply_fused_kernel(const FusedArgs p
       }
 
       // ---- shrink: split-K partials of this CTA's slice on tensor cores ----
+      // Transposed tiles: the slot's rank rows are the MMA's M side (16 per
+      // tile), the tile's tokens its N side. Within a 16-feature step the lane
+      // that owns MMA columns {2c, 2c+1, 2c+8, 2c+9} takes features 4c..4c+3
+      // of both operands (the sum over the step does not depend on the order),
+      // so every operand is one 8-byte shared-memory load per row. Rank rows
+      // past the rank (stale or unset shared memory) only reach partial
+      // columns >= rank, which the gather drops; token columns >= nt are zero.
       {
-        float acc[RM / 8][4];
+        constexpr int MT = RM / 16;
+        float acc0[MT][4], acc1[MT][4];
 #pragma unroll
-        for (int i = 0; i < RM / 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-        const int arow_l = lane & 15;
-        const int xrow = arow_l < nt ? arow_l : 0;  // rows past the tile repeat row 0
-        const uint32_t xa = sx_addr + (uint32_t)(xrow * kp + (lane >> 4) * 8) * 2u;
-        const int brow = lane & 7, bhalf = (lane >> 3) & 1;
-        if (ok) {
-          for (int kk = warp; kk < ksteps; kk += NW) {
-            uint32_t a0, a1, a2, a3;
-            ldsm_x4(xa + (uint32_t)kk * 32u, a0, a1, a2, a3);
+        for (int i = 0; i < MT; ++i)
 #pragma unroll
-            for (int i = 0; i < RM / 8; ++i) {
-              if (i * 8 < rank) {
-                uint32_t b0, b1;
-                ldsm_x2(sa_addr + (uint32_t)((i * 8 + brow) * kp + kk * 16 + bhalf * 8) * 2u, b0, b1);
-                mma_16816<T>(acc[i], a0, a1, a2, a3, b0, b1);
-              }
+          for (int e = 0; e < 4; ++e) acc0[i][e] = acc1[i][e] = 0.f;
+        const bool xv = g < nt;
+        auto kstep = [&](int kk, float (&acc)[MT][4]) {
+          const int kf = kk * 16 + 4 * cq;
+          uint2 xb = make_uint2(0u, 0u);
+          if (xv) xb = *reinterpret_cast<const uint2*>(s_x + (size_t)g * kp + kf);
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+            if (mt * 16 < rank) {
+              const uint2 lo = *reinterpret_cast<const uint2*>(s_a + (size_t)(mt * 16 + g) * kp + kf);
+              const uint2 hi = *reinterpret_cast<const uint2*>(s_a + (size_t)(mt * 16 + 8 + g) * kp + kf);
+              mma_16816<T>(acc[mt], lo.x, hi.x, lo.y, hi.y, xb.x, xb.y);
             }
           }
+        };
+        if (ok) {
+          // two accumulator chains (alternate steps) halve the dependent MMA chain
+          for (int kk = warp; kk < ksteps; kk += 2 * NW) {
+            kstep(kk, acc0);
+            if (kk + NW < ksteps) kstep(kk + NW, acc1);
+          }
         }
-        // rows g (< 8) of this warp's tiles -> warp partials
-        if (g < nt) {
+        // D[rank row][token]: rows g and g + 8 of each rank tile, tokens 2c and 2c + 1
 #pragma unroll
-          for (int i = 0; i < RM / 8; ++i) {
-            float* wr = s_wred + ((size_t)warp * TT + g) * RM + i * 8 + 2 * cq;
-            wr[0] = acc[i][0];
-            wr[1] = acc[i][1];
+        for (int u = 0; u < 2; ++u) {
+          const int t = 2 * cq + u;
+          if (t < nt) {
+            float* wr = s_wred + ((size_t)warp * TT + t) * RM;
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+              wr[mt * 16 + g] = acc0[mt][u] + acc1[mt][u];
+              wr[mt * 16 + 8 + g] = acc0[mt][2 + u] + acc1[mt][2 + u];
+            }
           }
         }
       }
@@ -386,19 +420,21 @@ __global__ void __launch_bounds__(kFusedNT) apply_fused_kernel(const FusedArgs p
             }
           }
         };
+        // per-lane rows (token g of the tile), hoisted out of the tile loop
+        T* const yrow = ybase + (int64_t)(g < nt ? s_rows[g] : 0) * m.y_stride + o_lo;
+        const T* const syrow = s_y + (size_t)g * p.ob_max;
+        const bool vec = m.y_tma != 0;
         auto tile_store = [&](int nb, const float (&acc)[4]) {
-          if (g < nt) {  // row g of the tile: outputs o, o + 1
+          if (g < nt) {  // row g of the tile: outputs ol, ol + 1 of the block
             const int ol = nb * 8 + 2 * cq;
-            const int o = o_lo + ol;
-            T* yp = ybase + (int64_t)s_rows[g] * m.y_stride + o;
-            if (o + 1 < o_hi && m.y_tma) {
-              const uint32_t u = *reinterpret_cast<const uint32_t*>(s_y + (size_t)g * p.ob_max + ol);
-              *reinterpret_cast<uint32_t*>(yp) =
-                  Pack2<T>::pack(Num<T>::from_f(round_to<T>(acc[0] * scale) + Pack2<T>::lo(u)),
-                                 Num<T>::from_f(round_to<T>(acc[1] * scale) + Pack2<T>::hi(u)));
+            const uint32_t d = pack_round2<T>(acc[0] * scale, acc[1] * scale);  // T(scaling * delta)
+            if (vec && ol + 1 < olen) {
+              const uint32_t u = *reinterpret_cast<const uint32_t*>(syrow + ol);
+              *reinterpret_cast<uint32_t*>(yrow + ol) =
+                  pack_round2<T>(Pack2<T>::lo(d) + Pack2<T>::lo(u), Pack2<T>::hi(d) + Pack2<T>::hi(u));
             } else {
-              if (o < o_hi) yp[0] = Num<T>::from_f(round_to<T>(acc[0] * scale) + ldcg_f<T>(yp));
-              if (o + 1 < o_hi) yp[1] = Num<T>::from_f(round_to<T>(acc[1] * scale) + ldcg_f<T>(yp + 1));
+              if (ol < olen) yrow[ol] = Num<T>::from_f(Pack2<T>::lo(d) + ldcg_f<T>(yrow + ol));
+              if (ol + 1 < olen) yrow[ol + 1] = Num<T>::from_f(Pack2<T>::hi(d) + ldcg_f<T>(yrow + ol + 1));
             }
           }
         };

@@ -82,6 +82,20 @@ struct Pack2<__half> {
   static __device__ __forceinline__ float hi(uint32_t u) { return __half2float(__ushort_as_half((unsigned short)(u >> 16))); }
 };
 
+// Two fp32 values rounded to T and packed (element 0 in the low half).
+template <typename T>
+__device__ __forceinline__ uint32_t pack_round2(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t pack_round2<__nv_bfloat16>(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+template <>
+__device__ __forceinline__ uint32_t pack_round2<__half>(float lo, float hi) {
+  const __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
 // Round an fp32 value through element type T and back (the value a tensor of
 // dtype T would hold).
 template <typename T>
