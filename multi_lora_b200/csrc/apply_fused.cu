@@ -149,9 +149,10 @@ struct FlatWalk {
 __host__ __device__ __forceinline__ int padded_row(int k) { return ((k / 8) % 2 == 0) ? k + 8 : k; }
 
 // RM: rank columns covered by the tiles (16, 32 or 64; >= R). Register caps
-// at RM 32 / 64 keep 4 / 3 CTAs per SM resident (no spills); RM 16 needs 48.
+// (48 / 64 / 85) keep 5 / 4 / 3 CTAs per SM resident, without spills; fewer
+// registers measured faster at RM 16 (the decode shapes are latency-bound).
 template <typename T, int RM>
-__global__ void __launch_bounds__(kFusedNT, RM == 16 ? 0 : RM == 32 ? 4 : 3) apply_fused_kernel(const FusedArgs p) {
+__global__ void __launch_bounds__(kFusedNT, RM == 16 ? 5 : RM == 32 ? 4 : 3) apply_fused_kernel(const FusedArgs p) {
   constexpr int NT = kFusedNT;
   constexpr int NW = NT / 32;
   constexpr int TT = kFusedTT;    // tokens per tile (MMA rows 8..15 repeat row 0 and are discarded)
@@ -159,7 +160,6 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? 0 : RM == 32 ? 4 : 3) app
   constexpr int MP = RM + 8;      // padded row of the bf16/f16 mid tile
   __shared__ FusedSegs sl;
   __shared__ int s_rows[TT];
-  __shared__ __align__(16) float s_part[TT][RM];
   __shared__ __align__(16) T s_mid[16][MP];
   __shared__ __align__(8) uint64_t bar_w, bar_p;
   extern __shared__ __align__(128) unsigned char s_dyn[];
@@ -319,15 +319,17 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? 0 : RM == 32 ? 4 : 3) app
 #pragma unroll
           for (int e = 0; e < 4; ++e) acc0[i][e] = acc1[i][e] = 0.f;
         const bool xv = g < nt;
-        auto kstep = [&](int kk, float (&acc)[MT][4]) {
-          const int kf = kk * 16 + 4 * cq;
+        // per-lane rows: token g of x, rank rows g and g + 8 of each rank tile
+        const T* const xl = s_x + (size_t)g * kp + 4 * cq;
+        const T* const al = s_a + (size_t)g * kp + 4 * cq;
+        auto kstep = [&](int off, float (&acc)[MT][4]) {  // off = first feature of the step
           uint2 xb = make_uint2(0u, 0u);
-          if (xv) xb = *reinterpret_cast<const uint2*>(s_x + (size_t)g * kp + kf);
+          if (xv) xb = *reinterpret_cast<const uint2*>(xl + off);
 #pragma unroll
           for (int mt = 0; mt < MT; ++mt) {
-            if (mt * 16 < rank) {
-              const uint2 lo = *reinterpret_cast<const uint2*>(s_a + (size_t)(mt * 16 + g) * kp + kf);
-              const uint2 hi = *reinterpret_cast<const uint2*>(s_a + (size_t)(mt * 16 + 8 + g) * kp + kf);
+            if (mt == 0 || mt * 16 < rank) {  // rank >= 1: the first rank tile always runs
+              const uint2 lo = *reinterpret_cast<const uint2*>(al + (size_t)(mt * 16) * kp + off);
+              const uint2 hi = *reinterpret_cast<const uint2*>(al + (size_t)(mt * 16 + 8) * kp + off);
               mma_16816<T>(acc[mt], lo.x, hi.x, lo.y, hi.y, xb.x, xb.y);
             }
           }
@@ -335,8 +337,8 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? 0 : RM == 32 ? 4 : 3) app
         if (ok) {
           // two accumulator chains (alternate steps) halve the dependent MMA chain
           for (int kk = warp; kk < ksteps; kk += 2 * NW) {
-            kstep(kk, acc0);
-            if (kk + NW < ksteps) kstep(kk + NW, acc1);
+            kstep(kk * 16, acc0);
+            if (kk + NW < ksteps) kstep((kk + NW) * 16, acc1);
           }
         }
         // D[rank row][token]: rows g and g + 8 of each rank tile, tokens 2c and 2c + 1
@@ -353,29 +355,27 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? 0 : RM == 32 ? 4 : 3) app
           }
         }
       }
-      __syncthreads();
-      for (int e = tid; e < nt * RM; e += NT) {
-        const int t = e / RM, k = e - t * RM;
-        float v = 0.f;
-#pragma unroll
-        for (int w = 0; w < NW; ++w) v += s_wred[((size_t)w * TT + t) * RM + k];
-        s_part[t][k] = v;
-      }
-      __syncthreads();  // s_part complete
+      __syncthreads();  // warp partials complete
       if (first) cluster_wait_acquire();  // every peer runs and has its barriers initialised
       first = false;
-      // ---- push this CTA's partials into slot j of every peer's receive buffer ----
+      // ---- push this CTA's partial (its warps' partials summed in warp order) into
+      //      slot j of every peer's receive buffer ----
       if (tid == 0) mbar_arrive_expect_tx(&bar_p, (uint32_t)cs * nt * RM * sizeof(float));
-      {
-        const uint32_t my_recv = smem_addr(s_recv + (size_t)j * TT * RM);
-        const uint32_t my_bar = smem_addr(&bar_p);
-        for (int e = tid; e < cs * nt * Q4; e += NT) {
-          const int q = e / (nt * Q4), r = e - q * (nt * Q4);
-          const int t = r / Q4, k4 = (r - t * Q4) * 4;
-          const float4 v = *reinterpret_cast<const float4*>(&s_part[t][k4]);
-          st_async_v4(cluster_map(my_recv + (uint32_t)(t * RM + k4) * 4u, (uint32_t)q), v.x, v.y, v.z, v.w,
-                      cluster_map(my_bar, (uint32_t)q));
+      if (tid < nt * Q4) {
+        const int t = tid / Q4, k4 = (tid - t * Q4) * 4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+          const float4 u = *reinterpret_cast<const float4*>(s_wred + ((size_t)w * TT + t) * RM + k4);
+          v.x += u.x;
+          v.y += u.y;
+          v.z += u.z;
+          v.w += u.w;
         }
+        const uint32_t dst = smem_addr(s_recv + ((size_t)j * TT + t) * RM + k4);
+        const uint32_t bar = smem_addr(&bar_p);
+        for (int q = 0; q < cs; ++q)
+          st_async_v4(cluster_map(dst, (uint32_t)q), v.x, v.y, v.z, v.w, cluster_map(bar, (uint32_t)q));
       }
       ok = mbar_wait(&bar_p, p_phase, p.status) && ok;
       p_phase ^= 1u;
@@ -390,11 +390,8 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? 0 : RM == 32 ? 4 : 3) app
         }
         s_mid[t][k] = Num<T>::from_f(v);
       }
-      __syncthreads();  // s_mid complete
-      if (m.y_tma && olen > 0) {  // y rows staged during the shrink and exchange
-        cp_async_wait<0>();
-        __syncthreads();
-      }
+      if (m.y_tma && olen > 0) cp_async_wait<0>();  // y rows staged during the shrink and exchange
+      __syncthreads();  // s_mid and the staged y rows complete
       // ---- expand: this CTA's output block on tensor cores, fused scaling + residual ----
       if (ok) {
         uint32_t am[RM / 16][4];
@@ -438,14 +435,55 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? 0 : RM == 32 ? 4 : 3) app
             }
           }
         };
-        // two output tiles per iteration: independent tensor-core chains overlap their latencies
-        for (int nb = warp; nb < ntiles; nb += 2 * NW) {
-          float acc0[4], acc1[4];
-          const bool two = nb + NW < ntiles;
-          tile_mma(nb, acc0);
-          if (two) tile_mma(nb + NW, acc1);
-          tile_store(nb, acc0);
-          if (two) tile_store(nb + NW, acc1);
+        if (vec && R % 16 == 0) {
+          // Common shape (aligned y rows, 16-column k-steps): the loop is
+          // issue-bound, so its addresses advance by fixed strides and no
+          // per-tile bound or shape test is left in it. Two output tiles per
+          // iteration: independent tensor-core chains overlap their latencies.
+          const uint32_t tile_bytes = 8u * (uint32_t)R * sizeof(T);
+          uint32_t ba = sb_addr + (uint32_t)((warp * 8 + brow) * R + bhalf * 8) * 2u;
+          T* yp = yrow + warp * 8 + 2 * cq;
+          const T* sp = syrow + warp * 8 + 2 * cq;
+          const bool lane_out = g < nt;
+          auto mma_at = [&](uint32_t baddr, float (&acc)[4]) {
+            acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+#pragma unroll
+            for (int kk = 0; kk < RM / 16; ++kk) {
+              if (RM == 16 || kk < ksteps_r) {  // rank >= 1: the first k-step always runs
+                uint32_t b0, b1;
+                ldsm_x2(baddr + (uint32_t)kk * 32u, b0, b1);
+                mma_16816<T>(acc, am[kk][0], am[kk][1], am[kk][2], am[kk][3], b0, b1);
+              }
+            }
+          };
+          auto store_at = [&](T* y, const T* sy, const float (&acc)[4]) {
+            const uint32_t d = pack_round2<T>(acc[0] * scale, acc[1] * scale);  // T(scaling * delta)
+            const uint32_t u = *reinterpret_cast<const uint32_t*>(sy);
+            *reinterpret_cast<uint32_t*>(y) =
+                pack_round2<T>(Pack2<T>::lo(d) + Pack2<T>::lo(u), Pack2<T>::hi(d) + Pack2<T>::hi(u));
+          };
+          for (int nb = warp; nb < ntiles; nb += 2 * NW) {
+            float acc0[4], acc1[4];
+            const bool two = nb + NW < ntiles;
+            mma_at(ba, acc0);
+            if (two) mma_at(ba + NW * tile_bytes, acc1);
+            if (lane_out) {
+              store_at(yp, sp, acc0);
+              if (two) store_at(yp + 8 * NW, sp + 8 * NW, acc1);
+            }
+            ba += 2 * NW * tile_bytes;
+            yp += 16 * NW;
+            sp += 16 * NW;
+          }
+        } else {
+          for (int nb = warp; nb < ntiles; nb += 2 * NW) {
+            float acc0[4], acc1[4];
+            const bool two = nb + NW < ntiles;
+            tile_mma(nb, acc0);
+            if (two) tile_mma(nb + NW, acc1);
+            tile_store(nb, acc0);
+            if (two) tile_store(nb + NW, acc1);
+          }
         }
       }
       const bool more = (q0 + TT < ntok) || (from + kFusedScan < p.bs);
