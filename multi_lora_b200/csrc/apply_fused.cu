@@ -57,8 +57,10 @@ struct FusedSegs {
 };
 
 // Warp 0 scans segment indices [from, min(bs, from + kFusedScan)) with every
-// load of the pass issued up front (one memory round trip).
-__device__ __forceinline__ void fused_scan(FusedSegs& sl, int slot, int from, const FusedArgs& p) {
+// load of the pass issued up front (one memory round trip). With `rows`, the
+// token rows of the pass's first kFusedTT tokens are written there too.
+__device__ __forceinline__ void fused_scan(FusedSegs& sl, int slot, int from, const FusedArgs& p,
+                                           int* rows = nullptr) {
   if (threadIdx.x >= 32) return;
   const int lane = threadIdx.x;
   constexpr int NB = kFusedScan / 32;
@@ -103,8 +105,11 @@ __device__ __forceinline__ void fused_scan(FusedSegs& sl, int slot, int from, co
     }
     if (match) {
       const int pos = n + __popc(m & ((1u << lane) - 1u));
+      const int q0 = total + incl - len;  // the segment's first token within the slot
       sl.start[pos] = st[b];
-      sl.cum[pos] = total + incl - len;
+      sl.cum[pos] = q0;
+      if (rows != nullptr)
+        for (int q = q0; q < q0 + len && q < kFusedTT; ++q) rows[q] = st[b] + (q - q0);
     }
     n += __popc(m);
     total += __shfl_sync(0xffffffffu, incl, 31);
@@ -187,7 +192,7 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? 5 : RM == 32 ? 4 : 3) app
       default: s_scale = __ldg(static_cast<const float*>(p.scalings) + slot); break;
     }
   }
-  fused_scan(sl, slot, 0, p);
+  fused_scan(sl, slot, 0, p, s_rows);  // also the first tile's token rows
   __syncthreads();
   int rank = s_rank;
   const float scale = s_scale;
@@ -264,6 +269,7 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? 5 : RM == 32 ? 4 : 3) app
   bool ok = true;
   uint32_t p_phase = 0;
   bool first = true;
+  bool b_pending = true;  // bar_w (the dense B block) not yet waited on
   for (int from = 0; from < p.bs; from += kFusedScan) {
     if (from > 0) {
       __syncthreads();
@@ -273,10 +279,11 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? 5 : RM == 32 ? 4 : 3) app
     const int ntok = sl.cum[sl.n];
     for (int q0 = 0; q0 < ntok; q0 += TT) {
       const int nt = min(TT, ntok - q0);
-      if (tid < nt) s_rows[tid] = fused_token_row(sl, q0 + tid);
-      if (klen % 16 != 0)
+      const bool scanned_rows = from == 0 && q0 == 0;  // written by the first scan (barrier passed)
+      if (!scanned_rows && tid < nt) s_rows[tid] = fused_token_row(sl, q0 + tid);
+      if (klen % 16 != 0)  // pad columns: disjoint from the x rows loaded below
         for (int e = tid; e < TT * 8; e += NT) s_x[(size_t)(e / 8) * kp + klen + (e % 8)] = Num<T>::from_f(0.f);
-      __syncthreads();
+      if (!scanned_rows) __syncthreads();
       if (m.y_tma && olen > 0) {  // this tile's y rows (output block), needed only by the expand
         for (FlatWalk w(tid, NT, olen / 8); w.r < nt; w.next())
           cp_async16(s_y + (size_t)w.r * p.ob_max + w.c * 8,
@@ -291,12 +298,9 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? 5 : RM == 32 ? 4 : 3) app
             *reinterpret_cast<uint4*>(s_x + (size_t)w.r * kp + w.c * 8) = v;
           }
       }
-      if (first) {
-        cp_async_wait<1>();  // the weights group (this tile's y group may still be in flight)
-        ok = mbar_wait(&bar_w, 0, p.status) && ok;
-      }
-      __syncthreads();  // x tile and weights complete
-      if (first && !b_dense) {  // B block: zero the stale columns past the rank once it has landed
+      if (first) cp_async_wait<1>();  // the weights group (this tile's y group may still be in flight)
+      __syncthreads();  // x tile and A rows complete
+      if (first && !b_dense) {  // B rows (cp.async, landed): zero the stale columns past the rank
         for (int e = tid; e < olen * (R - rank); e += NT) {
           const int row = e / (R - rank), c = rank + e % (R - rank);
           s_b[(size_t)row * R + c] = Num<T>::from_f(0.f);
@@ -390,8 +394,12 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? 5 : RM == 32 ? 4 : 3) app
         }
         s_mid[t][k] = Num<T>::from_f(v);
       }
+      if (b_pending) {  // the dense B block, needed from here on, landed during the shrink
+        ok = mbar_wait(&bar_w, 0, p.status) && ok;
+        b_pending = false;
+      }
       if (m.y_tma && olen > 0) cp_async_wait<0>();  // y rows staged during the shrink and exchange
-      __syncthreads();  // s_mid and the staged y rows complete
+      __syncthreads();  // s_mid, B and the staged y rows complete
       // ---- expand: this CTA's output block on tensor cores, fused scaling + residual ----
       if (ok) {
         uint32_t am[RM / 16][4];
@@ -494,10 +502,8 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? 5 : RM == 32 ? 4 : 3) app
   // Never leave with copies in flight into this CTA's shared memory: weights
   // that no tile consumed (a slot with no tokens past the first scan pass),
   // or copies whose wait timed out, are drained here (bounded again).
-  if (first) {
-    cluster_wait_acquire();  // pairs the prologue arrive
-    mbar_wait(&bar_w, 0, p.status);
-  }
+  if (first) cluster_wait_acquire();  // pairs the prologue arrive
+  if (b_pending) mbar_wait(&bar_w, 0, p.status);
   cp_async_wait<0>();
   if (!ok && tid == 0) mbar_wait(&bar_p, p_phase ^ 1u, p.status);  // ok is only cleared inside a tile
 }
