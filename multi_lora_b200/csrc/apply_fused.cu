@@ -614,8 +614,9 @@ template <typename T, int RM>
 cudaError_t launch_rm(FusedArgs a, cudaStream_t st, bool pdl) {
   auto& l = launcher<T, RM>();
   // Cluster size: fewest waves of CTAs for the whole launch (every slot counted,
-  // since which slots the batch uses is only known on the device), ties to the
-  // larger cluster (shorter per-CTA critical path).
+  // since which slots the batch uses is only known on the device); ties go to
+  // the size closest to 8 (8, 16, 4, 2): on B200, clusters of 16 at the same
+  // wave count measured slower (twice the CTAs and partial pushes per slot).
   int best_cs = 0, best_waves = 1 << 30;
   size_t best_smem = 0;
   FusedArgs best = a;
@@ -641,7 +642,8 @@ cudaError_t launch_rm(FusedArgs a, cudaStream_t st, bool pdl) {
     if (per_sm <= 0) continue;
     const long long ctas = (long long)c.n_mod * c.num_slots * cs;
     const int waves = (int)((ctas + (long long)sm_count() * per_sm - 1) / ((long long)sm_count() * per_sm));
-    if (waves < best_waves || (waves == best_waves && cs > best_cs)) {
+    auto pref = [](int c) { return c == 8 ? 0 : c == 16 ? 1 : c == 4 ? 2 : 3; };
+    if (waves < best_waves || (waves == best_waves && pref(cs) < pref(best_cs))) {
       c.ks = ks;
       c.ob_max = ob_max;
       best = c;
