@@ -566,8 +566,8 @@ __global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(cons
         if (g < nt) {  // y = T(T(scale * acc) + y), in place in the staged tile
           uint32_t* yp = reinterpret_cast<uint32_t*>(ys + g * OCP + nb * 8 + 2 * cq);
           const uint32_t u = *yp;
-          *yp = Pack2<T>::pack(Num<T>::from_f(round_to<T>(acc[0] * scale) + Pack2<T>::lo(u)),
-                               Num<T>::from_f(round_to<T>(acc[1] * scale) + Pack2<T>::hi(u)));
+          const uint32_t d = pack_round2<T>(acc[0] * scale, acc[1] * scale);  // T(scaling * delta)
+          *yp = pack_round2<T>(Pack2<T>::lo(d) + Pack2<T>::lo(u), Pack2<T>::hi(d) + Pack2<T>::hi(u));
         }
       };
       // two output tiles per iteration: independent tensor-core chains overlap their latencies

@@ -389,9 +389,10 @@ __global__ void __launch_bounds__(kTcThreads) lora_expand_tc_kernel(const __grid
           const uint32_t in[4] = {yin.x, yin.y, yin.z, yin.w};
           uint32_t o[4];
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            o[i] = Pack2<T>::pack(Num<T>::from_f(round_to<T>(v[8 * q + 2 * i] * scale) + Pack2<T>::lo(in[i])),
-                                  Num<T>::from_f(round_to<T>(v[8 * q + 2 * i + 1] * scale) + Pack2<T>::hi(in[i])));
+          for (int i = 0; i < 4; ++i) {  // y = T(T(scale * acc) + y), two values per packed rounding
+            const uint32_t d = pack_round2<T>(v[8 * q + 2 * i] * scale, v[8 * q + 2 * i + 1] * scale);
+            o[i] = pack_round2<T>(Pack2<T>::lo(d) + Pack2<T>::lo(in[i]), Pack2<T>::hi(d) + Pack2<T>::hi(in[i]));
+          }
           *reinterpret_cast<uint4*>(yrow + c * 32 + q * 8) = make_uint4(o[0], o[1], o[2], o[3]);
         }
       }
