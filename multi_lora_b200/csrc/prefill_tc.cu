@@ -375,17 +375,22 @@ __global__ void __launch_bounds__(kTcThreads) lora_expand_tc_kernel(const __grid
     default: scale = __ldg(static_cast<const float*>(p.scalings) + t.slot); break;
   }
   T* yrow = static_cast<T*>(mod.y) + (int64_t)(t.row0 + r) * mod.y_stride + n0;
+  // A whole tile (128 rows of this segment) is written back in place into the
+  // staged y boxes and stored with two TMA tensor stores; a ragged tile (its
+  // last rows belong to the next segment) stores its own rows with 16-byte stores.
+  const bool tma_out = t.rows == kTcTileM;
 #pragma unroll 1
   for (int c = 0; c < kTcBN / 32; ++c) {
     float v[32];
     tmem_ld32(taddr + ((uint32_t)(warp * 32) << 16) + (uint32_t)(c * 32), v);
     if (row_ok) {
-      const unsigned char* yb = s_y + (c >> 1) * Y_BYTES;
+      unsigned char* yb = s_y + (c >> 1) * Y_BYTES;
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const int col = (c & 1) * 32 + q * 8;  // column within the 64-column box
-        if (n0 + c * 32 + q * 8 < mod.out_dim) {
-          const uint4 yin = *reinterpret_cast<const uint4*>(yb + sw128_offset(r, col));
+        if (tma_out || n0 + c * 32 + q * 8 < mod.out_dim) {
+          uint4* ys = reinterpret_cast<uint4*>(yb + sw128_offset(r, col));
+          const uint4 yin = *ys;
           const uint32_t in[4] = {yin.x, yin.y, yin.z, yin.w};
           uint32_t o[4];
 #pragma unroll
@@ -393,9 +398,20 @@ __global__ void __launch_bounds__(kTcThreads) lora_expand_tc_kernel(const __grid
             const uint32_t d = pack_round2<T>(v[8 * q + 2 * i] * scale, v[8 * q + 2 * i + 1] * scale);
             o[i] = pack_round2<T>(Pack2<T>::lo(d) + Pack2<T>::lo(in[i]), Pack2<T>::hi(d) + Pack2<T>::hi(in[i]));
           }
-          *reinterpret_cast<uint4*>(yrow + c * 32 + q * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+          if (tma_out) *ys = make_uint4(o[0], o[1], o[2], o[3]);
+          else *reinterpret_cast<uint4*>(yrow + c * 32 + q * 8) = make_uint4(o[0], o[1], o[2], o[3]);
         }
       }
+    }
+  }
+  if (tma_out) {
+    fence_proxy_async_smem();  // the rows written above, to the TMA (async proxy)
+    __syncthreads();
+    if (tid == 0 && ok) {  // columns past out_dim are clipped by the tensor map
+      tma_store_2d(tc_map(p.y_map, m), n0, t.row0, s_y);
+      if (n0 + kTcBK < mod.out_dim) tma_store_2d(tc_map(p.y_map, m), n0 + kTcBK, t.row0, s_y + Y_BYTES);
+      bulk_commit();
+      bulk_wait_all();  // complete before the CTA (and its shared memory) goes away
     }
   }
   tc_fence_before();
