@@ -120,7 +120,7 @@ cudaError_t rms_dispatch(const RmsNormArgs& a, cudaStream_t st, bool pdl) {
   if (nchunk <= 64) return go(rmsnorm_kernel<T, V, 256, 32, 2>, 256, 32);
   if (nchunk <= 128) return go(rmsnorm_kernel<T, V, 256, 32, 4>, 256, 32);
   if (nchunk <= 256) return go(rmsnorm_kernel<T, V, 256, 64, 4>, 256, 64);
-  if (nchunk <= 512) return go(rmsnorm_kernel<T, V, 256, 128, 4>, 256, 128);
+  if (nchunk <= 512) return go(rmsnorm_kernel<T, V, 256, 256, 2>, 256, 256);
   if (nchunk <= 1024) return go(rmsnorm_kernel<T, V, 256, 256, 4>, 256, 256);
   if (nchunk <= 2048) return go(rmsnorm_kernel<T, V, 512, 512, 4>, 512, 512);
   return go(rmsnorm_kernel<T, V, 1024, 1024, 4>, 1024, 1024);  // loops blocks past 4096 chunks
