@@ -160,7 +160,7 @@ template <typename T, int RM>
 __global__ void __launch_bounds__(kFusedNT, RM == 16 ? 5 : RM == 32 ? 4 : 3) apply_fused_kernel(const FusedArgs p) {
   constexpr int NT = kFusedNT;
   constexpr int NW = NT / 32;
-  constexpr int TT = kFusedTT;    // tokens per tile (MMA rows 8..15 repeat row 0 and are discarded)
+  constexpr int TT = kFusedTT;    // tokens per tile (the shrink's MMA N; the expand's M rows 8..15 are zero)
   constexpr int Q4 = RM / 4;      // 16-byte pieces per partial row
   constexpr int MP = RM + 8;      // padded row of the bf16/f16 mid tile
   __shared__ FusedSegs sl;
