@@ -570,14 +570,55 @@ __global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(cons
           *yp = pack_round2<T>(Pack2<T>::lo(d) + Pack2<T>::lo(u), Pack2<T>::hi(d) + Pack2<T>::hi(u));
         }
       };
-      // two output tiles per iteration: independent tensor-core chains overlap their latencies
-      for (int nb = warp; nb < it.ocl / 8; nb += 2 * NC) {
-        float acc0[4], acc1[4];
-        const bool two = nb + NC < it.ocl / 8;
-        tile_mma(nb, acc0);
-        if (two) tile_mma(nb + NC, acc1);
-        tile_store(nb, acc0);
-        if (two) tile_store(nb + NC, acc1);
+      const int ntl = it.ocl / 8;
+      if (rank % 16 == 0) {
+        // Whole 16-column k-steps (every rank column is valid, no masks): the
+        // loop is issue-bound, so its addresses advance by fixed strides with
+        // no per-tile test. Two output tiles per iteration: independent
+        // tensor-core chains overlap their latencies.
+        const uint32_t tile_bytes = 8u * (uint32_t)p.R * sizeof(T);
+        uint32_t bad = ba + (uint32_t)((warp * 8 + brow) * p.R + bhalf * 8) * 2u;
+        T* yl = ys + g * OCP + warp * 8 + 2 * cq;
+        const bool lane_out = g < nt;
+        auto mma_at = [&](uint32_t baddr, float (&acc)[4]) {
+          acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+#pragma unroll
+          for (int kk = 0; kk < RM / 16; ++kk) {
+            if (RM == 16 || kk < ksteps) {  // rank >= 16 here: the first k-step always runs
+              uint32_t b0, b1;
+              ldsm_x2(baddr + (uint32_t)kk * 32u, b0, b1);
+              mma_16816<T>(acc, am[kk][0], am[kk][1], am[kk][2], am[kk][3], b0, b1);
+            }
+          }
+        };
+        auto store_at = [&](T* y, const float (&acc)[4]) {  // y = T(T(scale * acc) + y), in place
+          uint32_t* yp = reinterpret_cast<uint32_t*>(y);
+          const uint32_t u = *yp;
+          const uint32_t d = pack_round2<T>(acc[0] * scale, acc[1] * scale);
+          *yp = pack_round2<T>(Pack2<T>::lo(d) + Pack2<T>::lo(u), Pack2<T>::hi(d) + Pack2<T>::hi(u));
+        };
+        for (int nb = warp; nb < ntl; nb += 2 * NC) {
+          float acc0[4], acc1[4];
+          const bool two = nb + NC < ntl;
+          mma_at(bad, acc0);
+          if (two) mma_at(bad + NC * tile_bytes, acc1);
+          if (lane_out) {
+            store_at(yl, acc0);
+            if (two) store_at(yl + 8 * NC, acc1);
+          }
+          bad += 2 * NC * tile_bytes;
+          yl += 16 * NC;
+        }
+      } else {
+        // two output tiles per iteration: independent tensor-core chains overlap their latencies
+        for (int nb = warp; nb < ntl; nb += 2 * NC) {
+          float acc0[4], acc1[4];
+          const bool two = nb + NC < ntl;
+          tile_mma(nb, acc0);
+          if (two) tile_mma(nb + NC, acc1);
+          tile_store(nb, acc0);
+          if (two) tile_store(nb + NC, acc1);
+        }
       }
     }
     fence_proxy_async_smem();  // the y tile written above is read next by the bulk stores
