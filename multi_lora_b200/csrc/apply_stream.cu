@@ -335,39 +335,57 @@ __global__ void __launch_bounds__(kStreamThreads) lora_shrink_stream_kernel(cons
       const int m = item % p.n_mod;
       const int par = j & 1;
       const StreamTile t = stream_tile(rt, p.num_slots, item / p.n_mod);
-      float acc[RM / 8][4];
+      // Transposed tiles: the slot's rank rows are the MMA's M side (16 per
+      // tile), the tile's tokens its N side. Inside a 16-feature step the lane
+      // that owns MMA columns {2c, 2c+1, 2c+8, 2c+9} takes features 4c..4c+3
+      // of both operands (the step's sum does not depend on the order), so
+      // each operand is one 8-byte shared-memory load per row; two accumulator
+      // chains take alternate steps. Rank rows past the rank (stale stage
+      // rows) only reach partial columns >= rank, which are never written
+      // out; token columns >= nt are zero.
+      constexpr int MT = RM / 16;
+      float acc0[MT][4], acc1[MT][4];
 #pragma unroll
-      for (int i = 0; i < RM / 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-      const int xrow = (lane & 15) < t.nt ? (lane & 15) : 0;  // MMA rows past the tile repeat row 0
-      const int brow = lane & 7, bhalf = (lane >> 3) & 1;
+      for (int i = 0; i < MT; ++i)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc0[i][e] = acc1[i][e] = 0.f;
+      const bool xv = g < t.nt;
       for (int c = 0; c < cnt; ++c, ++f) {
         const int s = f % NS;
         if (ok) ok = mbar_wait(&full[s], (f / NS) & 1, p.status);  // after a timeout: no more waits
         if (ok) {
           const int ksteps = min(KC, p.in_dim - (c_lo + c) * KC) / 16;
-          const uint32_t xa = smem_addr(s_dyn + s * SS::BYTES + SS::A_BYTES) + (uint32_t)(xrow * KCP + (lane >> 4) * 8) * 2u;
-          const uint32_t aa = smem_addr(s_dyn + s * SS::BYTES);
-          for (int kk = warp; kk < ksteps; kk += NC) {
-            uint32_t a0, a1, a2, a3;
-            ldsm_x4(xa + (uint32_t)kk * 32u, a0, a1, a2, a3);
+          const T* xl = reinterpret_cast<const T*>(s_dyn + s * SS::BYTES + SS::A_BYTES) + g * KCP + 4 * cq;
+          const T* al = reinterpret_cast<const T*>(s_dyn + s * SS::BYTES) + g * KCP + 4 * cq;
+          auto kstep = [&](int off, float (&acc)[MT][4]) {  // off = first feature of the step
+            uint2 xb = make_uint2(0u, 0u);
+            if (xv) xb = *reinterpret_cast<const uint2*>(xl + off);
 #pragma unroll
-            for (int i = 0; i < RM / 8; ++i) {
-              if (i * 8 < t.rank) {
-                uint32_t b0, b1;
-                ldsm_x2(aa + (uint32_t)((i * 8 + brow) * KCP + kk * 16 + bhalf * 8) * 2u, b0, b1);
-                mma_16816<T>(acc[i], a0, a1, a2, a3, b0, b1);
+            for (int mt = 0; mt < MT; ++mt) {
+              if (mt == 0 || mt * 16 < t.rank) {  // rank >= 1: the first rank tile always runs
+                const uint2 lo = *reinterpret_cast<const uint2*>(al + mt * 16 * KCP + off);
+                const uint2 hi = *reinterpret_cast<const uint2*>(al + (mt * 16 + 8) * KCP + off);
+                mma_16816<T>(acc[mt], lo.x, hi.x, lo.y, hi.y, xb.x, xb.y);
               }
             }
+          };
+          for (int kk = warp; kk < ksteps; kk += 2 * NC) {
+            kstep(kk * 16, acc0);
+            if (kk + NC < ksteps) kstep((kk + NC) * 16, acc1);
           }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
       }
       // this CTA's partial: the warps' tiles summed in warp order ...
+      // (D[rank row][token]: rows g and g + 8 of each rank tile, tokens 2c and 2c + 1)
 #pragma unroll
-      for (int i = 0; i < RM / 8; ++i) {
-        s_red[warp][g][i * 8 + 2 * cq] = acc[i][0];
-        s_red[warp][g][i * 8 + 2 * cq + 1] = acc[i][1];
+      for (int u = 0; u < 2; ++u) {
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          s_red[warp][2 * cq + u][mt * 16 + g] = acc0[mt][u] + acc1[mt][u];
+          s_red[warp][2 * cq + u][mt * 16 + 8 + g] = acc0[mt][2 + u] + acc1[mt][2 + u];
+        }
       }
       named_barrier(1, NC * 32);
       // ... pushed into slot `crank` of CTA 0's receive buffer (once CTA 0 has
