@@ -71,7 +71,7 @@ struct ExpandStage {
   static constexpr int MP = RM + 8;
   static constexpr int B_BYTES = align128(OC * RM * 2 + 16);  // + slack: a half k-step may read 16 B past the block
   static constexpr int Y_BYTES = align128(kStreamTM * OCP * 2);
-  static constexpr int M_BYTES = align128(kStreamTM * MP * 2);
+  static constexpr int M_BYTES = align128(kStreamTM * MP * 4);  // rows of T, or of fp32 (mid_f32)
   static constexpr int BYTES = B_BYTES + Y_BYTES + M_BYTES;
 };
 
@@ -247,7 +247,7 @@ __device__ __forceinline__ StreamModule stream_module(const StreamArgs& p, int m
 // shrink
 // ---------------------------------------------------------------------------
 template <typename T, int RM>
-__global__ void __launch_bounds__(kStreamThreads) lora_shrink_stream_kernel(const StreamArgs p) {
+__global__ void __launch_bounds__(kStreamThreads, 1) lora_shrink_stream_kernel(const StreamArgs p) {
   using SS = ShrinkStage<RM>;
   constexpr int NC = kStreamConsumers, NS = kStreamShrinkStages, TM = kStreamTM, KS = kStreamShrinkSplit;
   constexpr int KC = SS::KC, KCP = SS::KCP;
@@ -414,13 +414,14 @@ __global__ void __launch_bounds__(kStreamThreads) lora_shrink_stream_kernel(cons
         if (ctid == 0) mbar_arrive_expect_tx(&bar_red[par], (uint32_t)KS * PB);
         if (ok) ok = mbar_wait(&bar_red[par], (j >> 1) & 1, p.status);
         if (ok) {
-          T* mid = static_cast<T*>(p.mid) + m * p.R;
           for (int e = ctid; e < t.nt * t.rank; e += NC * 32) {
             const int r = e / t.rank, k = e - r * t.rank;
             float v = 0.f;
 #pragma unroll
             for (int q = 0; q < KS; ++q) v += s_recv[par][q][r][k];
-            mid[(int64_t)rt.tok[t.start + r] * p.mid_stride + k] = Num<T>::from_f(v);
+            const int64_t at = (int64_t)rt.tok[t.start + r] * p.mid_stride + m * p.R + k;
+            if (p.mid_f32) static_cast<float*>(p.mid)[at] = v;  // a partial, summed across ranks later
+            else static_cast<T*>(p.mid)[at] = Num<T>::from_f(v);
           }
         }
         named_barrier(1, NC * 32);  // done reading s_recv[par]
@@ -499,6 +500,7 @@ __global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(cons
   auto stage_b = [&](int s) { return reinterpret_cast<T*>(s_dyn + s * ES::BYTES); };
   auto stage_y = [&](int s) { return reinterpret_cast<T*>(s_dyn + s * ES::BYTES + ES::B_BYTES); };
   auto stage_m = [&](int s) { return reinterpret_cast<T*>(s_dyn + s * ES::BYTES + ES::B_BYTES + ES::Y_BYTES); };
+  const uint32_t mid_es = p.mid_f32 ? 4u : (uint32_t)sizeof(T);  // bytes per mid element
 
   if (warp == NC) {
     // ---------------- producer warp: lane 0 arms the stage, every lane issues copies ----------------
@@ -506,7 +508,8 @@ __global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(cons
       const int s = j % NS;
       const Item it = decode(j);
       if (lane == 0) {
-        mbar_arrive_expect_tx(&full[s], (uint32_t)(it.ocl * p.R + it.t.nt * it.ocl + it.t.nt * p.R) * sizeof(T));
+        mbar_arrive_expect_tx(&full[s], (uint32_t)(it.ocl * p.R + it.t.nt * it.ocl) * sizeof(T) +
+                                            (uint32_t)it.t.nt * p.R * mid_es);
         const T* b = static_cast<const T*>(it.m.b) + ((int64_t)it.t.slot * it.m.out_dim + it.o0) * p.R;
         bulk_copy_g2s(stage_b(s), b, (uint32_t)it.ocl * p.R * sizeof(T), &full[s]);
       }
@@ -521,6 +524,9 @@ __global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(cons
         const int t = r >> 1;
         const int64_t row = rt.tok[it.t.start + t];
         if ((r & 1) == 0) bulk_copy_g2s(stage_y(s) + t * OCP, y + row * it.m.y_stride, it.ocl * sizeof(T), &full[s]);
+        else if (p.mid_f32)  // fp32 rows (MP floats apart in the stage)
+          bulk_copy_g2s(reinterpret_cast<float*>(stage_m(s)) + t * MP,
+                        static_cast<const float*>(p.mid) + row * p.mid_stride + it.mi * p.R, p.R * 4u, &full[s]);
         else bulk_copy_g2s(stage_m(s) + t * MP, mid + row * p.mid_stride, p.R * sizeof(T), &full[s]);
       }
     };
@@ -551,9 +557,22 @@ __global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(cons
       uint32_t am[RM / 16][4];
       const int mrow = (lane & 15) < nt ? (lane & 15) : 0;
       const uint32_t ma = smem_addr(stage_m(s)) + (uint32_t)(mrow * MP + (lane >> 4) * 8) * 2u;
+      const float* mf = reinterpret_cast<const float*>(stage_m(s)) + g * MP + 2 * cq;  // fp32 rows (mid_f32)
 #pragma unroll
       for (int kk = 0; kk < RM / 16; ++kk) {
-        ldsm_x4(ma + (uint32_t)kk * 32u, am[kk][0], am[kk][1], am[kk][2], am[kk][3]);
+        if (p.mid_f32) {  // fragment built from fp32 rows, each pair rounded to T (rows g < nt; g + 8 >= nt)
+          float2 v0 = make_float2(0.f, 0.f), v2 = v0;
+          if (g < nt) {
+            v0 = *reinterpret_cast<const float2*>(mf + kk * 16);
+            v2 = *reinterpret_cast<const float2*>(mf + kk * 16 + 8);
+          }
+          am[kk][0] = pack_round2<T>(v0.x, v0.y);
+          am[kk][1] = 0u;
+          am[kk][2] = pack_round2<T>(v2.x, v2.y);
+          am[kk][3] = 0u;
+        } else {
+          ldsm_x4(ma + (uint32_t)kk * 32u, am[kk][0], am[kk][1], am[kk][2], am[kk][3]);
+        }
         const int c0 = kk * 16 + 2 * cq, c1 = c0 + 8;
         const uint32_t m0 = (c0 < rank ? 0x0000ffffu : 0u) | (c0 + 1 < rank ? 0xffff0000u : 0u);
         const uint32_t m1 = (c1 < rank ? 0x0000ffffu : 0u) | (c1 + 1 < rank ? 0xffff0000u : 0u);
@@ -697,6 +716,8 @@ cudaError_t launch_stream_rm(const StreamArgs& a, cudaStream_t st, bool pdl) {
   auto ke = lora_expand_stream_kernel<T, RM>;
   if (!ensure_smem(ks, smem_s, set_s, mu) || !ensure_smem(ke, smem_e, set_e, mu)) return cudaErrorNotSupported;
   const dim3 grid(stream_sm_count());
+  if (a.phase == 2)  // expand only: mid comes from the caller (e.g. all-reduced shrink partials)
+    return launch_kernel(ke, grid, dim3(kStreamThreads), smem_e, st, pdl, a);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(stream_sm_count() / kStreamShrinkSplit * kStreamShrinkSplit));
   cfg.blockDim = dim3(kStreamThreads);
@@ -712,7 +733,7 @@ cudaError_t launch_stream_rm(const StreamArgs& a, cudaStream_t st, bool pdl) {
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   cudaError_t e = cudaLaunchKernelEx(&cfg, ks, a);
-  if (e != cudaSuccess) return e;
+  if (e != cudaSuccess || a.phase == 1) return e;
   // the expand kernel always follows with the programmatic attribute: its wait is the shrink -> expand edge
   return launch_kernel(ke, grid, dim3(kStreamThreads), smem_e, st, true, a);
 }
@@ -725,7 +746,7 @@ constexpr int kStreamMaxRoutingBytes = 48 * 1024;
 // then uses another one).
 cudaError_t launch_apply_stream(const StreamArgs& a, int dtype, cudaStream_t st, bool pdl) {
   if (dtype != kBF16 && dtype != kF16) return cudaErrorNotSupported;
-  if (a.n_mod < 1 || a.n_mod > kMaxStreamModules || a.R > 64 || a.R % 8 != 0 || a.in_dim % 16 != 0)
+  if (a.n_mod < 1 || a.n_mod > kMaxStreamModules || a.R > 64 || a.R % 8 != 0 || (a.phase != 2 && a.in_dim % 16 != 0))
     return cudaErrorNotSupported;
   if (stream_routing_bytes(a.num_slots, a.S) > kStreamMaxRoutingBytes) return cudaErrorNotSupported;
   const int rm = a.R <= 16 ? 16 : a.R <= 32 ? 32 : 64;

@@ -112,6 +112,40 @@ int mlora_sgemm_lora_a_fwd(const void* x, int64_t rows, int64_t in_dim, int64_t 
   if (x == nullptr || weights == nullptr || output == nullptr)
     return fail(MLORA_ERR_INVALID_ARGUMENT, "x / weights / output is NULL");
 
+  // Large decode batches: the streaming shrink kernel alone (its fp32 output
+  // mode is the tensor-parallel shrink partial), as mlora_apply_lora chooses it.
+  const int forced = apply_path_override();
+  const bool stream_pref = forced == 3 || (forced != 2 && rows >= 256 && meta->max_len <= 64);
+  if (stream_pref && es == 2 && stack_num == 1 && in_dim % 16 == 0 && max_rank % 8 == 0 && max_rank <= 64 &&
+      aligned(x, 16) && x_row_stride % 8 == 0 && aligned(weights, 16) && rows <= INT32_MAX) {
+    mlora::StreamArgs sa{};
+    sa.x = x;
+    sa.x_stride = x_row_stride;
+    sa.n_mod = 1;
+    sa.mod[0].a = weights;
+    sa.mid = output;
+    sa.mid_stride = output_row_stride;
+    sa.mid_f32 = out_f32 ? 1 : 0;
+    sa.phase = 1;
+    sa.seg_indptr = meta->seg_indptr;
+    sa.weight_indices = meta->weight_indices;
+    sa.lora_ranks = meta->lora_ranks;
+    sa.scalings = meta->scalings;
+    sa.scalings_dtype = meta->scalings_dtype;
+    sa.bs = meta->bs;
+    sa.S = (int)rows;
+    sa.in_dim = (int)in_dim;
+    sa.R = (int)max_rank;
+    sa.num_slots = meta->num_slots;
+    sa.status = status;
+    const cudaError_t e = mlora::launch_apply_stream(sa, dtype, (cudaStream_t)stream, pdl_on());
+    if (e == cudaSuccess) {
+      g_last_apply_path = 3;
+      return MLORA_OK;
+    }
+    if (e != cudaErrorNotSupported) return cuda_status(e, "streaming shrink launch");
+  }
+
   mlora::ShrinkArgs a{};
   a.x = x;
   a.x_stride = x_row_stride;
@@ -132,6 +166,7 @@ int mlora_sgemm_lora_a_fwd(const void* x, int64_t rows, int64_t in_dim, int64_t 
   a.status = status;
   const int V = 16 / es;
   a.vec_ok = (in_dim % V == 0) && (x_row_stride % V == 0) && aligned(x, 16) && aligned(weights, 16);
+  g_last_apply_path = 2;
   return cuda_status(mlora::launch_shrink(a, dtype, out_f32, (cudaStream_t)stream, pdl_on()), "shrink launch");
 }
 
@@ -158,6 +193,43 @@ int mlora_sgemm_lora_b_fwd(const void* mid, int64_t rows, int64_t mid_row_stride
   if (mid == nullptr || weights == nullptr || y == nullptr)
     return fail(MLORA_ERR_INVALID_ARGUMENT, "mid / weights / y is NULL");
 
+  // Large decode batches: the streaming expand kernel alone. An fp32 mid (the
+  // all-reduced tensor-parallel shrink partials) is rounded to the activation
+  // dtype as the kernel loads it, as the reference rounds mid before the product.
+  const int forced = apply_path_override();
+  const bool stream_pref = forced == 3 || (forced != 2 && rows >= 256 && meta->max_len <= 64);
+  const int mid_es = mid_f32 ? 4 : es;
+  if (stream_pref && es == 2 && max_rank % 8 == 0 && max_rank <= 64 && out_dim % 8 == 0 && aligned(y, 16) &&
+      y_row_stride % 8 == 0 && aligned(weights, 16) && aligned(mid, 16) && (mid_row_stride * mid_es) % 16 == 0 &&
+      rows <= INT32_MAX) {
+    mlora::StreamArgs sa{};
+    sa.n_mod = 1;
+    sa.mod[0].b = weights;
+    sa.mod[0].y = y;
+    sa.mod[0].y_stride = y_row_stride;
+    sa.mod[0].out_dim = (int)out_dim;
+    sa.mid = const_cast<void*>(mid);
+    sa.mid_stride = mid_row_stride;
+    sa.mid_f32 = mid_f32 ? 1 : 0;
+    sa.phase = 2;
+    sa.seg_indptr = meta->seg_indptr;
+    sa.weight_indices = meta->weight_indices;
+    sa.lora_ranks = meta->lora_ranks;
+    sa.scalings = meta->scalings;
+    sa.scalings_dtype = meta->scalings_dtype;
+    sa.bs = meta->bs;
+    sa.S = (int)rows;
+    sa.R = (int)max_rank;
+    sa.num_slots = meta->num_slots;
+    sa.status = status;
+    const cudaError_t e = mlora::launch_apply_stream(sa, dtype, (cudaStream_t)stream, pdl_on());
+    if (e == cudaSuccess) {
+      g_last_apply_path = 3;
+      return MLORA_OK;
+    }
+    if (e != cudaErrorNotSupported) return cuda_status(e, "streaming expand launch");
+  }
+
   mlora::ExpandArgs a{};
   a.mid = mid;
   a.mid_stride = mid_row_stride;
@@ -180,6 +252,7 @@ int mlora_sgemm_lora_b_fwd(const void* mid, int64_t rows, int64_t mid_row_stride
   const int V = 16 / es;
   a.vec_ok = (max_rank % V == 0) && aligned(weights, 16);
   a.y_vec_ok = (y_row_stride % 2 == 0) && aligned(y, 2 * es);
+  g_last_apply_path = 2;
   return cuda_status(mlora::launch_expand(a, dtype, mid_f32, (cudaStream_t)stream, pdl_on()), "expand launch");
 }
 
@@ -347,6 +420,7 @@ int apply_impl(const void* x, int64_t rows, int64_t in_dim, int64_t x_row_stride
                                 y_row_strides[i], dtype, status, stream);
     if (rc != MLORA_OK) return rc;
   }
+  g_last_apply_path = 2;  // separate shrink and expand launches, whichever kernels they took
   return MLORA_OK;
 }
 

@@ -117,6 +117,8 @@ struct StreamArgs {
   int scalings_dtype;
   int bs, S, in_dim, R, num_slots;
   uint32_t* status;
+  int phase;              // 0: shrink then expand; 1: shrink only; 2: expand only
+  int mid_f32;            // 1: mid holds fp32 (the shrink writes unrounded sums, the expand rounds them to T)
 };
 cudaError_t launch_apply_stream(const StreamArgs& a, int dtype, cudaStream_t st, bool pdl);
 

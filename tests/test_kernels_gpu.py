@@ -123,6 +123,56 @@ def _check_case(c, dev, dtype, scal_dtype=torch.float32):
         np.testing.assert_allclose(m[rows, :r], mid_want[:, :r], rtol=tol_m, atol=tol_m)
 
 
+STREAM_OP_SHAPES = [
+    # n_in, n_out, R, ranks, lens: 256 rows or more of short segments
+    (4096, 1024, 16, [16] * 8 + [0], [1] * 300),                # decode-sized, a base (rank-0) slot
+    (1024, 768, 32, [32, 8, 17, 24], [1] * 200 + [3] * 30),     # ranks < max_rank (NaN tails), multi-token segments
+]
+
+
+@pytest.mark.parametrize("mid_dtype", [torch.bfloat16, torch.float32], ids=["mid_bf16", "mid_f32"])
+@pytest.mark.parametrize("shape", STREAM_OP_SHAPES, ids=lambda s: f"{s[0]}x{s[1]}r{s[2]}")
+def test_standalone_shrink_and_expand_take_streaming_kernels(cuda_dev, shape, mid_dtype):
+    """mlora_sgemm_lora_a_fwd / _b_fwd at 256+ rows run the streaming kernels
+    alone. An fp32 mid is the tensor-parallel shrink partial: written unrounded
+    by the shrink, rounded to bf16 by the expand as it loads it."""
+    n_in, n_out, R, ranks, lens = shape
+    c = _case(hash((n_in, n_out, R, 5)) % 1000, torch.bfloat16, n_in, n_out, R, ranks, lens, cuda_dev)
+    S = c["x"].shape[0]
+    meta = C.make_meta(c["lens"], c["widx"], c["ranks"], c["scal"], cuda_dev)
+    mid_big = torch.full((S, R + 8), -3.0, dtype=mid_dtype, device=cuda_dev)  # 16-byte rows, sentinel past R
+    mid = mid_big[:, :R]
+    p0, p1 = c["pad"]
+    y = c["big"][p0:p0 + S, p1:p1 + n_out]
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_dev)
+    C.check(C.shrink(c["x"], c["A"], meta, mid, status=status))
+    assert _native.capi().mlora_last_apply_path() == 3
+    C.check(C.expand(mid, c["B"], meta, y, status=status))
+    assert _native.capi().mlora_last_apply_path() == 3
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    ind = meta.seg_indptr.cpu().numpy()
+    A32, B32 = np.nan_to_num(C.f32(c["A"])), np.nan_to_num(C.f32(c["B"]))
+    want = O.apply_lora_fp32(C.f32(c["x"]), A32, B32, ind, c["widx"], c["ranks"], c["scal"], len(c["lens"]),
+                             C.f32(c["ybase"]))
+    got = C.f32(y)
+    assert np.isfinite(got).all()
+    np.testing.assert_allclose(got, want, rtol=RTOL, atol=ATOL)
+    big = C.f32(c["big"])
+    inner = np.zeros(big.shape, bool)
+    inner[p0:p0 + S, p1:p1 + n_out] = True
+    assert (big[~inner] == 7.0).all()
+    m = C.f32(mid_big)
+    assert (m[:, R:] == -3.0).all()
+    tol_m = 1e-3 if mid_dtype == torch.float32 else 1e-2
+    for seg, slot in enumerate(c["widx"]):
+        r = c["ranks"][slot]
+        rows = slice(ind[seg], ind[seg + 1])
+        assert (m[rows, r:R] == -3.0).all()  # columns past the rank, and rank-0 segments, untouched
+        mid_want = C.f32(c["x"])[rows] @ A32[slot, :r].T
+        np.testing.assert_allclose(m[rows, :r], mid_want, rtol=tol_m, atol=tol_m)
+
+
 SHAPES = [
     # n_in, n_out, R, ranks, lens
     (4096, 4096, 16, [16] * 6, [1] * 24),                       # decode, cfg2-like module
