@@ -211,7 +211,7 @@ int mlora_version(void);
  * (1 = one fused launch, 2 = shrink + expand launches, 3 = the streaming
  * shrink/expand kernel pair, 4 = the tensor-core (tcgen05) shrink/expand pair
  * for long segments, 0 = none yet). mlora_sgemm_lora_a_fwd / _b_fwd set it
- * too: 3 when they ran the streaming kernel (rows >= 256 of short segments,
+ * too: 3 when they ran the streaming kernel (segments of at most 64 rows,
  * bf16/f16, aligned operands), 2 for the general kernel. */
 int mlora_last_apply_path(void);
 
