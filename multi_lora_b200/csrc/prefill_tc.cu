@@ -411,7 +411,7 @@ __global__ void __launch_bounds__(kTcThreads) lora_expand_tc_kernel(const __grid
       tma_store_2d(tc_map(p.y_map, m), n0, t.row0, s_y);
       if (n0 + kTcBK < mod.out_dim) tma_store_2d(tc_map(p.y_map, m), n0 + kTcBK, t.row0, s_y + Y_BYTES);
       bulk_commit();
-      bulk_wait_all();  // complete before the CTA (and its shared memory) goes away
+      bulk_wait_read_all();  // the boxes are read before the CTA (and its shared memory) goes away
     }
   }
   tc_fence_before();
