@@ -1,8 +1,8 @@
 """Generate the golden fixtures in this directory by running the REFERENCE's own code.
 
-Runs only in the build container, where the reference project is mounted
-(default /root/reference; override with MLORA_REFERENCE). The fixtures are
-committed; tests never import the reference.
+Runs only where a checkout of the reference project is available; point
+MLORA_REFERENCE at its root. The fixtures are committed; tests never import
+the reference.
 
 What produces each fixture (paths within the reference project):
 * toy_f32.npz        — cfg1: backend/torch_backend.py
@@ -22,7 +22,7 @@ What produces each fixture (paths within the reference project):
 * pool.json, pool_slots.npz — pool.LoRAMemoryPool on the CPU (LRU and FIFO):
                        residency, evictions, batch info and slot contents.
 
-    python tests/golden/make_golden.py
+    MLORA_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 """
 
 from __future__ import annotations
@@ -35,7 +35,9 @@ import types
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("MLORA_REFERENCE", "/root/reference"))
+if not os.environ.get("MLORA_REFERENCE"):
+    sys.exit("set MLORA_REFERENCE to the root of a reference checkout")
+REF = Path(os.environ["MLORA_REFERENCE"])
 
 if os.environ.get("PYTHONHASHSEED") != "0" or os.environ.get("TRITON_INTERPRET") != "1":
     env = dict(os.environ, PYTHONHASHSEED="0", TRITON_INTERPRET="1")
