@@ -46,7 +46,7 @@ namespace cg = cooperative_groups;
 namespace mlora {
 
 constexpr int kFusedNT = 256;
-constexpr int kFusedTT = 8;       // tokens per tile
+constexpr int kFusedTT = 6;       // tokens per tile (6: a q/k/v CTA fits 4 per SM; 7+ tokens in a slot are rare in decode)
 constexpr int kFusedScan = 256;   // segment indices scanned per pass
 
 // Segment list of one slot for up to kFusedScan scanned segment indices.
@@ -160,7 +160,7 @@ template <typename T, int RM>
 __global__ void __launch_bounds__(kFusedNT, RM == 16 ? 5 : RM == 32 ? 4 : 3) apply_fused_kernel(const FusedArgs p) {
   constexpr int NT = kFusedNT;
   constexpr int NW = NT / 32;
-  constexpr int TT = kFusedTT;    // tokens per tile (the shrink's MMA N; the expand's M rows 8..15 are zero)
+  constexpr int TT = kFusedTT;    // tokens per tile (the shrink's MMA N; the expand's M rows TT..15 are zero)
   constexpr int Q4 = RM / 4;      // 16-byte pieces per partial row
   constexpr int MP = RM + 8;      // padded row of the bf16/f16 mid tile
   __shared__ FusedSegs sl;
