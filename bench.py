@@ -78,8 +78,9 @@ WORKLOADS = {
                              "bf16", 4096, 1024, 14336, 32, 4340, 8, 64, 128, requests=8),
     "cfg4": Workload("cfg4", "Heavy-tail decode with eviction: Llama-2-7B shapes, 32 layers, 256 adapters of rank "
                              "{8,16,32,64} (alpha 2r), 64-slot pool (max_rank 64, LRU), 256 tokens/step with Zipf(1.1) "
-                             "adapter ids, admission: tokens in draw order until 64 distinct adapters, the rest "
-                             "deferred to the next step; pinned-host slot loads; RMSNorm on; bf16",
+                             "adapter ids, admission (multi_lora_b200.admission): deferred tokens first, then tokens whose "
+                             "adapter is resident, then the rest, while at most 64 adapters are named; the others "
+                             "wait for the next step; pinned-host slot loads; RMSNorm on; bf16",
                      4096, 4096, 11008, 32, 256, 256, 64, 128),
     "cfg5": Workload("cfg5", "Llama-3-70B-shaped decode: 80 layers x 7 LoRA projections + 2 RMSNorm, 512 tokens, "
                              "128 adapters r16 (alpha 32), bf16", 8192, 1024, 28672, 80, 512, 128, 16, 32),
@@ -353,6 +354,13 @@ class CpuReference:
         be.apply_lora(self.xd, A["down"], B["down"], y["down"])
         return time.perf_counter() - t0
 
+    def step(self, layers: int) -> float:
+        """Seconds for one step of ``layers`` layers."""
+        t0 = time.perf_counter()
+        for _ in range(layers):
+            self.layer()
+        return time.perf_counter() - t0
+
     def measure(self, seconds: float = 12.0) -> dict:
         self.layer()
         n, el = 0, 0.0
@@ -367,24 +375,22 @@ class CpuReference:
                 "per_layer_ms": round(per_layer * 1e3, 3)}
 
 
+REF_BUDGET_S = 240.0  # wall-clock bound of the reference arm's warm-up + timed steps
+
 POOL_SLOTS = 64
 ZIPF_S = 1.1
 CFG4_RANKS = (8, 16, 32, 64)
 CFG4_TEMPLATES = 8  # distinct host weight sets per rank (adapters share them; every load still copies its bank)
 
 
-def admit(queue: list, slots: int):
-    """cfg4 admission: tokens in queue order join the batch while their adapter
-    is already admitted or fewer than ``slots`` adapters are; the others are
-    deferred (returned in order) to the next step."""
-    admitted, deferred, distinct = [], [], set()
-    for name in queue:
-        if name in distinct or len(distinct) < slots:
-            distinct.add(name)
-            admitted.append(name)
-        else:
-            deferred.append(name)
-    return admitted, deferred, distinct
+def admit(queue: list, slots: int, resident=(), n_deferred: int = 0, resident_first: bool = False):
+    """cfg4 admission through the library's AdmissionPolicy: returns (admitted names
+    in queue order, deferred names in retry order, admitted adapters)."""
+    from multi_lora_b200.admission import AdmissionPolicy
+
+    adm = AdmissionPolicy(slots, resident_first=resident_first).admit(queue, resident=resident,
+                                                                      n_deferred=n_deferred)
+    return [queue[i] for i in adm.admitted], [queue[i] for i in adm.deferred], adm.adapters
 
 
 def module_keys(layers: int):
@@ -454,7 +460,7 @@ def run_pool_workload(args, wl: Workload, dev) -> None:
         L.x = {"q": L.xn1, "k": L.xn1, "v": L.xn1, "o": xo, "gate": L.xn2, "up": L.xn2, "down": xd}
         layers.append(L)
 
-    # Zipf(s) over the adapters; admission in draw order until 64 distinct, the rest deferred
+    # Zipf(s) over the adapters; AdmissionPolicy picks the tokens (at most 64 adapters), the rest deferred
     p_zipf = 1.0 / np.arange(1, wl.adapters + 1) ** ZIPF_S
     p_zipf /= p_zipf.sum()
     pending: list = []
@@ -462,7 +468,9 @@ def run_pool_workload(args, wl: Workload, dev) -> None:
     def next_batch():
         nonlocal pending
         draws = list(rng.choice(wl.adapters, size=T - len(pending), p=p_zipf))
-        admitted, pending, distinct = admit(pending + [f"a{int(i)}" for i in draws], POOL_SLOTS)
+        admitted, pending, distinct = admit(pending + [f"a{int(i)}" for i in draws], POOL_SLOTS,
+                                            resident=pool.name_to_slot.keys(), n_deferred=len(pending),
+                                            resident_first=args.resident_first)
         return admitted, distinct
 
     be = CudaLoRABackend()
@@ -536,7 +544,8 @@ def run_pool_workload(args, wl: Workload, dev) -> None:
                     "loads_per_step": round(stats["loads"] / args.steps, 2),
                     "h2d_gb_per_step": round(per_step_h2d / 1e9, 3),
                     "h2d_gbs_achieved": round(per_step_h2d / (ms / 1e3) / 1e9, 1),
-                    "compute_ms_per_step_alone": round(compute_ms, 4), "deferred_at_end": len(pending)},
+                    "compute_ms_per_step_alone": round(compute_ms, 4), "deferred_at_end": len(pending),
+                    "admission": "resident-first" if args.resident_first else "queue order"},
            "e2e": {"value": round(value, 1), "unit": UNIT, "h2d_bytes_per_step": round(per_step_h2d),
                    "d2h_bytes_per_step": 0, "path": "admission + pool.prepare_lora_batch (evict, pinned H2D, "
                                                     "scatter) + routing write + graph replay, every step"},
@@ -557,7 +566,8 @@ def config_block(wl: Workload, n: int) -> dict:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default 400 for this library, 20 for the reference's CPU path)")
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg2")
@@ -565,9 +575,13 @@ def main() -> None:
                     help="override the workload's layer count (small cases for profiler captures only; "
                          "the reported numbers are then not the workload's)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--resident-first", action=argparse.BooleanOptionalAction, default=True,
+                    help="cfg4: admit tokens whose adapter is resident before the others (fewer loads)")
     ap.add_argument("--ungrouped", action="store_true",
                     help="one apply_lora call per projection instead of grouping q/k/v and gate/up")
     args = ap.parse_args()
+    if args.steps is None:
+        args.steps = 20 if args.impl == "reference" else 400
     wl = WORKLOADS[args.workload]
     if args.layers > 0:
         wl.layers = args.layers
@@ -579,21 +593,34 @@ def main() -> None:
     n = max(args.gpus, world)
 
     if args.impl == "reference":
-        # the reference's CPU path on the host cores; rank 0 alone
+        # the reference's CPU path on the host cores; rank 0 alone. Each timed
+        # step runs every layer of the workload (2 RMSNorms + 7 projections per
+        # layer), so steps x ms_per_step is the time actually spent; only when
+        # that would pass REF_BUDGET_S does a step shrink to fewer layers, and
+        # the line then says so (config.layers is what one step ran).
         if rank != 0:
             return
         ref = CpuReference(wl)
+        est = ref.layer()  # one layer sizes the run
+        layers = wl.layers
+        if (args.steps + args.warmup) * wl.layers * est > REF_BUDGET_S:
+            layers = max(1, int(REF_BUDGET_S / ((args.steps + args.warmup) * est)))
         for _ in range(args.warmup):
-            ref.layer()
-        per_layer = statistics.mean(ref.layer() for _ in range(args.steps))
-        value = wl.tokens / (wl.layers * per_layer)
+            ref.step(layers)
+        times = [ref.step(layers) for _ in range(args.steps)]
+        ms = statistics.mean(times) * 1e3
+        value = wl.tokens / (ms / 1e3)
+        cfg = config_block(wl, n)
+        sample = f"each step: {layers} {wl.name} layers (2 RMSNorm + 7 projections each, bf16, unsharded)"
+        if layers != wl.layers:
+            cfg["layers"] = layers
+            cfg["workload"] += f" [reference step shortened to {layers} of {wl.layers} layers to fit the run budget]"
         out = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": n,
-               "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_layer * wl.layers * 1e3,
+               "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-               "data": "synthetic", "config": config_block(wl, n),
+               "data": "synthetic", "config": cfg,
                "cpu_baseline": {"value": value, "unit": UNIT, "cores": ref.threads, "kind": "port",
-                                "sample": f"each step: one {wl.name} layer (2 RMSNorm + 7 projections, unsharded), "
-                                          f"x{wl.layers} layers"},
+                                "sample": sample},
                "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(out), flush=True)
         return

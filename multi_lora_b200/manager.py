@@ -16,6 +16,7 @@ from typing import Dict, Iterable, List, Optional
 import torch
 import torch.nn as nn
 
+from multi_lora_b200.admission import Admission, AdmissionPolicy
 from multi_lora_b200.backend.base import LoRABackend
 from multi_lora_b200.backend.registry import get_lora_backend
 from multi_lora_b200.batch_info import (
@@ -88,6 +89,31 @@ class MultiLoRAManager:
             raise ValueError(f"invalid lora batch: distinct={len(set(lora_names))} max={self.max_loras_per_batch}")
         self.pool.prepare_lora_batch(set(lora_names), weight_store=self._weight_store)
         return self.pool.build_batch_info(list(lora_names))
+
+    def admit_tokens(self, lora_names: List[LoraName], *, n_deferred: int = 0, max_tokens: Optional[int] = None,
+                     resident_first: bool = True) -> Admission:
+        """Choose which queued tokens run this step so that they name at most
+        ``max_loras_per_batch`` adapters (the reference raises instead,
+        manager.py:172-180). ``lora_names[i]`` is token i's adapter; the first
+        ``n_deferred`` are tokens deferred by earlier steps (admitted first),
+        then tokens whose adapter is resident in the pool, then the rest
+        (rule in :mod:`multi_lora_b200.admission`)."""
+        policy = AdmissionPolicy(self.max_loras_per_batch, resident_first=resident_first)
+        return policy.admit(lora_names, resident=self.pool.name_to_slot.keys(), n_deferred=n_deferred,
+                            max_tokens=max_tokens)
+
+    def prefetch_lora_batch(self, lora_names: Iterable[LoraName]) -> None:
+        """Start the loads of a coming step's adapters now, before its metadata is built.
+
+        The loads run on the pool's copy stream; a load into a slot that
+        already-enqueued work reads waits only for that work (per-slot events),
+        so the H2D overlaps the step in flight. The compute stream waits for the
+        loads before anything enqueued after this call. The coming step's
+        ``build_kernel_input_metadata`` then finds the adapters resident."""
+        names = set(lora_names)
+        if not validate_lora_batch(list(names), max_loras_per_batch=self.max_loras_per_batch):
+            raise ValueError(f"invalid lora batch: distinct={len(names)} max={self.max_loras_per_batch}")
+        self.pool.prepare_lora_batch(names, weight_store=self._weight_store)
 
     @torch.inference_mode()
     def build_kernel_input_metadata(self, lora_names: List[LoraName], *, seq_lens: List[int]) -> KernelInputMetaData:
