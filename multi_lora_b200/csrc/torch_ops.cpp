@@ -268,6 +268,34 @@ at::Tensor rmsnorm(const at::Tensor& x, const at::Tensor& weight, double eps) {
   return rmsnorm_out(x, weight, eps, out);
 }
 
+// Slot-load scatter (scatter_bank.py:68-93 of the reference): every block of
+// the h staged banks into its slot. `rects` is a CUDA int64 [n, 6] table of
+// mlora_scatter_rect_t rows (src_offset, dst address, slot_stride, rows, cols,
+// dst_row_stride); the destinations are the pool's slot stacks, addressed by
+// device pointer as the reference's tables do.
+void scatter_stage(const at::Tensor& stage, const at::Tensor& slots, const at::Tensor& rects, int64_t max_rect_elems,
+                   const c10::optional<at::Tensor>& status) {
+  const at::Device dev = stage.device();
+  check_cuda(stage, "stage", dev);
+  check_cuda(slots, "slots", dev);
+  check_cuda(rects, "rects", dev);
+  TORCH_CHECK(stage.dim() == 2 && stage.is_contiguous(), "mlora: stage must be a contiguous [h, total] tensor");
+  TORCH_CHECK(slots.scalar_type() == at::kLong && slots.dim() == 1 && slots.is_contiguous(),
+              "mlora: slots must be a contiguous int64 [h] tensor");
+  TORCH_CHECK(slots.numel() <= stage.size(0), "mlora: ", slots.numel(), " slots for ", stage.size(0), " stage rows");
+  TORCH_CHECK(rects.scalar_type() == at::kLong && rects.dim() == 2 && rects.size(1) == 6 && rects.is_contiguous(),
+              "mlora: rects must be a contiguous int64 [n, 6] tensor");
+  TORCH_CHECK(max_rect_elems >= 0, "mlora: max_rect_elems must be >= 0");
+  static_assert(sizeof(mlora_scatter_rect_t) == 6 * sizeof(int64_t), "rect layout");
+  const c10::cuda::CUDAGuard guard(dev);
+  const int rc = mlora_scatter_stage(stage.data_ptr(), stage.size(1), (int32_t)slots.numel(),
+                                     reinterpret_cast<const int64_t*>(slots.data_ptr()),
+                                     reinterpret_cast<const mlora_scatter_rect_t*>(rects.data_ptr()),
+                                     (int32_t)rects.size(0), max_rect_elems, dt_code(stage.scalar_type()),
+                                     status_ptr(status, dev), at::cuda::getCurrentCUDAStream().stream());
+  check_rc(rc);
+}
+
 }  // namespace
 
 TORCH_LIBRARY(mlora, m) {
@@ -289,6 +317,7 @@ TORCH_LIBRARY(mlora, m) {
       "Tensor(b!)? mid=None, Tensor(c!)? status=None) -> ()");
   m.def("rmsnorm(Tensor x, Tensor weight, float eps) -> Tensor");
   m.def("rmsnorm_out(Tensor x, Tensor weight, float eps, Tensor(a!) out) -> Tensor(a!)");
+  m.def("scatter_stage(Tensor stage, Tensor slots, Tensor rects, int max_rect_elems, Tensor(a!)? status=None) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(mlora, CUDA, m) {
@@ -298,4 +327,5 @@ TORCH_LIBRARY_IMPL(mlora, CUDA, m) {
   m.impl("apply_lora_group", &apply_lora_group);
   m.impl("rmsnorm", &rmsnorm);
   m.impl("rmsnorm_out", &rmsnorm_out);
+  m.impl("scatter_stage", &scatter_stage);
 }

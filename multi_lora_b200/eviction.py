@@ -16,7 +16,7 @@ _KINDS = ("lru", "fifo")
 class EvictionPolicy:
     def __init__(self, kind: str = "lru") -> None:
         if kind not in _KINDS:
-            raise ValueError(f"unknown eviction policy: {kind}; try lru | fifo")
+            raise ValueError(f"eviction policy {kind!r} is not one of {', '.join(_KINDS)}")
         self.kind = kind
         self.order: "OrderedDict[str, None]" = OrderedDict()  # front = evicted first
         self.eviction_count = 0
@@ -30,6 +30,7 @@ class EvictionPolicy:
             self.order.setdefault(name, None)
 
     def select_victim(self, candidates: Set[Optional[str]]) -> Optional[str]:
+        """Oldest queued name among ``candidates``; the base model only when no adapter is a candidate."""
         for name in self.order:
             if name in candidates:
                 self.eviction_count += 1
@@ -37,7 +38,7 @@ class EvictionPolicy:
         if None in candidates:
             self.eviction_count += 1
             return None
-        raise RuntimeError(f"no evictable adapter in {candidates}")
+        raise RuntimeError(f"none of the {len(candidates)} candidate(s) {sorted(map(str, candidates))} can be evicted")
 
     def remove(self, name: Optional[str]) -> None:
         if name is not None:

@@ -9,7 +9,8 @@ Loads (pool.py:157-316): each adapter's weights are packed once into a
 pinned host "bank" (all A blocks, then all B blocks, one layout per rank);
 a swap-in is one contiguous ``cudaMemcpyAsync`` of the bank into a device
 stage row on a private copy stream, then one scatter launch per chunk of
-adapters writes every block into its slot (``mlora_scatter_stage``). The
+adapters writes every block into its slot (``torch.ops.mlora.scatter_stage``
+over the C ABI's ``mlora_scatter_stage``). The
 compute stream waits on the copy stream's event, so the H2D overlaps
 whatever compute was queued before the load.
 
@@ -19,7 +20,6 @@ weights and loads nothing.
 
 from __future__ import annotations
 
-import ctypes
 from typing import Dict, List, Optional, Set, Tuple
 
 import torch
@@ -33,6 +33,8 @@ LoraName = Optional[str]
 
 # adapters staged per scatter launch (pool.py:18-20 uses the same chunking)
 _BANK_CHUNK = 4
+# attribute under which an AdapterWeights carries (layout, pinned bank)
+_BANK_ATTR = "_mlora_bank"
 
 
 class _RankPlan:
@@ -99,9 +101,7 @@ class _GpuBuffers:
         self.dims: Dict[str, Tuple[int, int]] = {}  # key -> (in, out)
         self._copy_stream: Optional[torch.cuda.Stream] = None
         self._load_event: Optional[torch.cuda.Event] = None
-        self._banks: Dict[int, tuple] = {}  # id(weights) -> (weights, rank, pinned flat)
-        self._plans: Dict[int, _RankPlan] = {}
-        self._plan_keys: Optional[tuple] = None
+        self._plans: Dict[tuple, _RankPlan] = {}  # (rank, module keys) -> bank layout
         self.release_modules = True  # drop the per-module host tensors once banked
         self._stage: Optional[torch.Tensor] = None
         self._status: Optional[torch.Tensor] = None
@@ -168,8 +168,7 @@ class _GpuBuffers:
         by_rank: Dict[int, list] = {}
         for slot, w in pairs:
             by_rank.setdefault(w.rank, []).append((slot, w))
-        lib = _native.capi()
-        dt = _native.dtype_code(self.dtype)
+        ops = _native.ops()
         stream = torch.cuda.current_stream(self.device)
         for rank, group in by_rank.items():
             plan = self._plan_for(rank)
@@ -181,54 +180,55 @@ class _GpuBuffers:
                     stage[i].copy_(self._bank_for(w, plan), non_blocking=True)
                 slots = torch.tensor([s for s, _ in chunk], dtype=torch.int64).pin_memory()
                 slots = slots.to(self.device, non_blocking=True)
-                rc = lib.mlora_scatter_stage(
-                    ctypes.c_void_p(stage.data_ptr()), plan.total, len(chunk), ctypes.c_void_p(slots.data_ptr()),
-                    ctypes.c_void_p(tables["rects"].data_ptr()), tables["n"], tables["max_numel"], dt,
-                    ctypes.c_void_p(self._status_word().data_ptr()), ctypes.c_void_p(stream.cuda_stream))
-                _native.check(rc)
+                ops.scatter_stage(stage[: len(chunk)], slots, tables["rects"], tables["max_numel"],
+                                  self._status_word())
                 slots.record_stream(stream)
 
     def _plan_for(self, rank: int) -> _RankPlan:
-        """Layout for ``rank``; every plan and bank is dropped when the module set changes."""
-        keys = tuple(self.dims)
-        if keys != self._plan_keys:
-            self._plans.clear()
-            self._banks.clear()
-            self._plan_keys = keys
-        plan = self._plans.get(rank)
+        """Bank layout for ``rank`` over the modules known now (one object per (rank, module set))."""
+        key = (rank, tuple(self.dims))
+        plan = self._plans.get(key)
         if plan is None:
-            plan = _RankPlan(rank, list(keys), self.dims)
-            self._plans[rank] = plan
+            plan = self._plans[key] = _RankPlan(rank, list(key[1]), self.dims)
         return plan
 
     def _bank_for(self, weights: AdapterWeights, plan: _RankPlan) -> torch.Tensor:
-        """The adapter's pinned bank for ``plan``, packed on first use and cached.
+        """The adapter's pinned bank in ``plan``'s layout.
 
-        Modules the adapter lacks are zero in the bank, so their slot's
-        leading ``rank`` rows/columns are cleared on load (pool.py:260-299).
+        The adapter object carries its bank with the layout it was packed for.
+        A bank for another layout (the pool learned new modules since) is
+        repacked block by block from the old bank, so an adapter whose module
+        tensors were released can still follow a growing module set; only an
+        adapter with neither tensors nor a bank cannot be packed. Modules the
+        adapter lacks are zero in the bank, so a load clears the leading
+        ``rank`` rows/columns of its slot there (pool.py:260-299 of the
+        reference).
         """
-        ent = self._banks.get(id(weights))
-        if ent is not None and ent[0] is weights and ent[1] == plan.rank:
-            return ent[2]
-        if weights.flattened:
-            raise RuntimeError(
-                f"adapter (rank {plan.rank}) was packed and its module tensors released; "
-                f"the bank cannot be rebuilt for a changed set of {len(plan.keys)} modules")
-        flat = torch.zeros(plan.total, dtype=self.dtype, pin_memory=not self.routing_only)
-        for key in plan.keys:
-            mod = weights.modules.get(key)
-            if mod is None:
-                continue
-            a, b = mod
-            na = plan.a_shape[key][0] * plan.a_shape[key][1]
-            nb = plan.b_shape[key][0] * plan.b_shape[key][1]
-            flat[plan.a_off[key]: plan.a_off[key] + na].copy_(a.reshape(-1).to(self.dtype))
-            flat[plan.b_off[key]: plan.b_off[key] + nb].copy_(b.reshape(-1).to(self.dtype))
-        self._banks[id(weights)] = (weights, plan.rank, flat)
-        if self.release_modules:
+        held = getattr(weights, _BANK_ATTR, None)
+        if held is not None and held[0] is plan:
+            return held[1]
+        bank = torch.zeros(plan.total, dtype=self.dtype, pin_memory=not self.routing_only)
+        if held is not None:
+            old_plan, old = held
+            for key in plan.keys:
+                if key not in old_plan.a_off:
+                    continue
+                for off, old_off, (r, c) in ((plan.a_off[key], old_plan.a_off[key], plan.a_shape[key]),
+                                             (plan.b_off[key], old_plan.b_off[key], plan.b_shape[key])):
+                    bank[off: off + r * c].copy_(old[old_off: old_off + r * c])
+        elif weights.flattened:
+            raise RuntimeError(f"adapter (rank {plan.rank}) has neither module tensors nor a packed bank")
+        else:
+            for key, (a, b) in weights.modules.items():
+                if key not in plan.a_off:
+                    continue
+                for off, t in ((plan.a_off[key], a), (plan.b_off[key], b)):
+                    bank[off: off + t.numel()].copy_(t.reshape(-1).to(self.dtype))
+        object.__setattr__(weights, _BANK_ATTR, (plan, bank))
+        if self.release_modules and weights.modules:
             weights.modules = {}
             weights.flattened = True
-        return flat
+        return bank
 
     def _ensure_stage(self, total: int) -> torch.Tensor:
         """Device stage [_BANK_CHUNK, total], one flat buffer reused across ranks."""

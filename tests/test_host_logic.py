@@ -146,3 +146,33 @@ def test_rank_plan_layout_tiles_bank():
         assert lo == pos
         pos = hi
     assert pos == plan.total
+
+
+def test_bank_repacks_from_old_bank_when_modules_grow():
+    """An adapter whose module tensors were released follows a growing module set:
+    its bank is repacked from the previous bank, with zeros for modules it lacks."""
+    from multi_lora_b200.pool import _GpuBuffers
+
+    bufs = _GpuBuffers(4, 4, torch.device("cpu"), torch.float32)
+    g = torch.Generator().manual_seed(3)
+    a1, b1 = torch.randn(4, 16, generator=g), torch.randn(24, 4, generator=g)
+    w = AdapterWeights(rank=4, scaling=1.0, modules={"q": (a1.clone(), b1.clone())})
+    bufs.ensure(w)
+    plan1 = bufs._plan_for(4)
+    bank1 = bufs._bank_for(w, plan1)
+    assert w.flattened and w.modules == {}
+    assert bufs._bank_for(w, plan1) is bank1  # cached for the same layout
+    # another adapter brings a new module: the layout grows, w is repacked from its bank
+    a2, b2 = torch.randn(4, 8, generator=g), torch.randn(40, 4, generator=g)
+    bufs.ensure(AdapterWeights(rank=4, scaling=1.0, modules={"down": (a2, b2)}))
+    plan2 = bufs._plan_for(4)
+    assert plan2 is not plan1 and plan2.total > plan1.total
+    bank2 = bufs._bank_for(w, plan2)
+    assert torch.equal(bank2[plan2.a_off["q"]: plan2.a_off["q"] + 64], a1.reshape(-1))
+    assert torch.equal(bank2[plan2.b_off["q"]: plan2.b_off["q"] + 96], b1.reshape(-1))
+    assert not bank2[plan2.a_off["down"]: plan2.a_off["down"] + 32].any()
+    assert not bank2[plan2.b_off["down"]: plan2.b_off["down"] + 160].any()
+    # an adapter with neither tensors nor a bank cannot be packed
+    bare = AdapterWeights(rank=4, scaling=1.0, modules={}, flattened=True)
+    with pytest.raises(RuntimeError):
+        bufs._bank_for(bare, plan2)

@@ -83,8 +83,7 @@ def test_pool_rounds_like_reference_gpu_test(cuda_dev, dtype):
         pool.prepare_lora_batch(names, weight_store=store)
         torch.cuda.synchronize()
         _check_resident(pool, ref)
-    assert len(pool.buffers._banks) <= len(store)
-    assert all(store[n].flattened for n in store)
+    assert all(store[n].flattened and hasattr(store[n], "_mlora_bank") for n in store)
     pool.buffers.check_status()
 
 
@@ -138,3 +137,50 @@ def test_load_into_unused_slot_overlaps_queued_compute(cuda_dev):
     overlapped = not torch.cuda.current_stream().query()  # ... while the queued compute still runs
     torch.cuda.synchronize()
     assert overlapped
+
+
+def test_scatter_stage_op_matches_oracle(cuda_dev):
+    """torch.ops.mlora.scatter_stage (the slot-load op, scatter_bank.py:68-93) writes
+    every staged block into its slot bit-exactly; entries past the rank stay as they were."""
+    from multi_lora_b200 import _native
+    from multi_lora_b200.pool import _RankPlan
+    from oracle import lora_oracle as O
+
+    dims = {"q": (24, 16), "down": (40, 24), "v": (16, 8)}  # key -> (in, out)
+    keys, rank, R, K = list(dims), 4, 8, 6
+    g = torch.Generator().manual_seed(11)
+    A = {k: torch.randn(K, R, dims[k][0], generator=g) for k in keys}
+    B = {k: torch.randn(K, dims[k][1], R, generator=g) for k in keys}
+    A_dev = {k: v.to(cuda_dev) for k, v in A.items()}
+    B_dev = {k: v.to(cuda_dev) for k, v in B.items()}
+
+    class _Bufs:
+        pass
+
+    bufs = _Bufs()
+    bufs.A, bufs.B = A_dev, B_dev
+    plan = _RankPlan(rank, keys, dims)
+    rects = torch.tensor(plan.rects(bufs), dtype=torch.int64, device=cuda_dev)
+    max_elems = max(r[3] * r[4] for r in plan.rects(bufs))
+    slots = [4, 1, 3]
+    banks = []
+    for i, _ in enumerate(slots):
+        mods = {k: (torch.randn(rank, dims[k][0], generator=g), torch.randn(dims[k][1], rank, generator=g))
+                for k in keys if not (i == 1 and k == "v")}  # adapter 1 lacks "v": zero blocks
+        banks.append(O.build_bank(rank, keys, dims, {k: (a.numpy(), b.numpy()) for k, (a, b) in mods.items()}))
+    stage = torch.tensor(np.stack(banks), device=cuda_dev)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_dev)
+    _native.ops().scatter_stage(stage, torch.tensor(slots, dtype=torch.int64, device=cuda_dev), rects, max_elems,
+                                status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    A_ref = {k: v.numpy().copy() for k, v in A.items()}
+    B_ref = {k: v.numpy().copy() for k, v in B.items()}
+    for bank, s in zip(banks, slots):
+        O.scatter_bank(bank, rank, keys, dims, A_ref, B_ref, s)
+    for k in keys:
+        np.testing.assert_array_equal(A_dev[k].cpu().numpy(), A_ref[k], err_msg=k)
+        np.testing.assert_array_equal(B_dev[k].cpu().numpy(), B_ref[k], err_msg=k)
+    with pytest.raises(RuntimeError):  # slots must be int64
+        _native.ops().scatter_stage(stage, torch.tensor(slots, dtype=torch.int32, device=cuda_dev), rects,
+                                    max_elems, status)
