@@ -208,6 +208,59 @@ def run_step(wl: Workload, layers, be, parts=("rmsnorm", "lora"), grouped=True, 
                     be.apply_lora(L.x[n], L.A[n], L.B[n], L.y[n])
 
 
+def tp_parity_check(wl: Workload, dev, be, tp_rank: int, tp: int, seed: int = 4242) -> dict:
+    """One checked layer at N > 1: the tensor-parallel result equals the unsharded one.
+
+    Every rank builds the same full-size layer (one seed), computes the
+    unsharded apply_lora of each projection on its own GPU (the 1-GPU path),
+    then runs the tensor-parallel path on its shards: column-parallel
+    projections write their output columns (all-gathered), row-parallel ones
+    add their columns of the delta into a partial output that is ybase on
+    rank 0 and zero elsewhere (all-reduced, as the model's own row-parallel
+    all-reduce would). Bound: max-abs 2e-2 / relative 1e-2, the bf16 bound of
+    this path. Returns {"parity": "ok" | "mismatch", "max_abs_err": ...}.
+    """
+    import torch.distributed as dist
+
+    from multi_lora_b200.tensor_parallel import row_parallel_apply, shard_bounds, shard_lora_stacks
+
+    g = torch.Generator(device=dev).manual_seed(seed)
+    dt = torch.bfloat16
+    T, K, R = wl.tokens, wl.adapters, wl.rank
+    worst, ok = 0.0, True
+    for name, n_in, n_out, kind in wl.projs:
+        if name not in ("q", "o", "gate", "down"):  # one projection of each shape class
+            continue
+        A = ((torch.rand(K, R, n_in, generator=g, device=dev) * 2 - 1) / math.sqrt(n_in)).to(dt)
+        B = (torch.randn(K, n_out, R, generator=g, device=dev) * 0.02).to(dt)
+        x = torch.randn(T, n_in, generator=g, device=dev).to(dt)
+        ybase = torch.randn(T, n_out, generator=g, device=dev).to(dt)
+        want = ybase.clone()
+        be.apply_lora(x, A, B, want)
+        a_sh, b_sh = shard_lora_stacks(A, B, kind, tp_rank, tp)
+        lo, hi = shard_bounds(n_out, tp_rank, tp)
+        if kind == COLUMN:
+            y_loc = ybase[:, lo:hi].contiguous()
+            be.apply_lora(x, a_sh, b_sh, y_loc)
+            parts = [torch.empty_like(y_loc) for _ in range(tp)]
+            dist.all_gather(parts, y_loc)
+            got = torch.cat(parts, dim=1)
+        else:
+            ilo, ihi = shard_bounds(n_in, tp_rank, tp)
+            y_part = ybase.clone() if tp_rank == 0 else torch.zeros_like(ybase)
+            row_parallel_apply(be, x[:, ilo:ihi].contiguous(), a_sh, b_sh, y_part, tp_rank, tp)
+            dist.all_reduce(y_part)
+            got = y_part
+        torch.cuda.synchronize()
+        err = (got.float() - want.float()).abs()
+        worst = max(worst, float(err.max()))
+        ok = ok and bool((err <= 2e-2 + 1e-2 * want.float().abs()).all())
+    flag = torch.tensor([1 if ok else 0], device=dev)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    return {"parity": "ok" if int(flag.item()) == 1 else "mismatch", "max_abs_err": round(worst, 6),
+            "checked": "q, gate (column-parallel) and o, down (row-parallel), one full-size layer, vs unsharded"}
+
+
 APPLY_PATH_NAMES = {1: "fused", 2: "split", 3: "stream", 4: "tc"}
 APPLY_KERNELS = {1: "apply_fused_kernel", 2: "shrink_kernel+expand_kernel",
                  3: "lora_shrink_stream_kernel+lora_expand_stream_kernel",
@@ -661,6 +714,17 @@ def main() -> None:
         torch.distributed.all_reduce(w)
     torch.cuda.synchronize()
 
+    parity = None
+    if world > 1:  # one checked layer before anything is timed
+        parity = tp_parity_check(wl, dev, be, rank, tp)
+        if parity["parity"] != "ok":
+            if rank == 0:
+                print(json.dumps({"metric": METRIC, "error": "tensor-parallel parity mismatch", **parity}),
+                      flush=True)
+            torch.distributed.destroy_process_group()
+            raise SystemExit(3)
+        be.set_kernel_input_metadata(meta)
+
     grouped = not args.ungrouped
     graphs = []
     step_graph = capture(lambda: run_step(wl, layers, be, grouped=grouped, tp=tp, tp_rank=rank))
@@ -778,6 +842,9 @@ def main() -> None:
                "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
                "clocks": clk, "pdl": _native.get_pdl(), "grouped": grouped,
                "apply_path": APPLY_PATH_NAMES.get(path, str(path))}
+        if parity is not None:
+            out["parity"] = parity["parity"]
+            out["parity_check"] = parity
         print(json.dumps(out), flush=True)
     # graphs that hold NCCL calls go before the process group
     del step_graph, g_lora, g_rms

@@ -142,7 +142,10 @@ int mlora_apply_lora_group(const void* x, int64_t rows, int64_t in_dim, int64_t 
  * max_rank 16); larger calls return MLORA_ERR_INVALID_ARGUMENT.
  * Every GPU that loads the library holds the 1 MiB until the process exits.
  * The first call on a device looks up the array's device address (with that
- * device current); make that first call before any stream capture. All calls
+ * device current) and caches it with the current context; a call in another
+ * context on that device (after cudaDeviceReset, or a non-primary context
+ * made current through the driver API) looks it up again. Make the first call
+ * in a context before any stream capture. All calls
  * on a device share the array: calls that overlap on the GPU race and give
  * wrong results. Nothing in it needs to start at zero.
  * This entry point has no counterpart in the reference project.
