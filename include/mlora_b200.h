@@ -168,6 +168,21 @@ int mlora_rmsnorm_fwd(const void* x, int64_t rows, int64_t hidden, int64_t strid
                       void* y, int64_t y_row_stride, float eps, int32_t dtype, void* stream);
 
 /*
+ * Residual add fused with RMSNorm, for the add that precedes a decoder
+ * layer's norm (hidden = residual + hidden; residual = hidden; norm(hidden)):
+ *   residual[r, :] = dtype(residual[r, :] + x[r, :])                 (in place)
+ *   y[r, :]        = dtype(res_f32 * rsqrt(mean(res_f32^2) + eps) * w_f32)
+ * with res_f32 the rounded sum just written. Bit-identical to an add in
+ * `dtype` followed by mlora_rmsnorm_fwd, in one pass over the row. Rows of x,
+ * residual and y are dense with the given row strides (elements). Replaces
+ * the separate residual add + rmsnorm_fwd pair the reference plans to fuse
+ * (OPTIMIZATION_TODO.md:125-142, task T22; kernels/rmsnorm.py:48-92).
+ */
+int mlora_fused_add_rmsnorm_fwd(const void* x, int64_t x_row_stride, void* residual, int64_t residual_row_stride,
+                                int64_t rows, int64_t hidden, const void* w, int32_t w_dtype, void* y,
+                                int64_t y_row_stride, float eps, int32_t dtype, void* stream);
+
+/*
  * One block of a staged adapter bank and where it goes in the slot stacks.
  * Source: `rows` x `cols` dense elements at `src_offset` within a stage row.
  * Destination: element [row, col] of slot s lands at

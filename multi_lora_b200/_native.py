@@ -64,6 +64,8 @@ CAPI_SIGNATURES = {
                                               ctypes.POINTER(_I64), ctypes.POINTER(_P), ctypes.POINTER(_I64), _I64,
                                               ctypes.POINTER(MetadataT), _I32, _P, _P]),
     "mlora_rmsnorm_fwd": (_I32, [_P, _I64, _I64, _I64, _I64, _I64, _P, _I32, _P, _I64, ctypes.c_float, _I32, _P]),
+    "mlora_fused_add_rmsnorm_fwd": (_I32, [_P, _I64, _P, _I64, _I64, _I64, _P, _I32, _P, _I64, ctypes.c_float,
+                                           _I32, _P]),
     "mlora_scatter_stage": (_I32, [_P, _I64, _I32, _P, _P, _I32, _I64, _I32, _P, _P]),
     "mlora_set_pdl": (None, [ctypes.c_int]),
     "mlora_get_pdl": (ctypes.c_int, []),

@@ -483,6 +483,42 @@ int mlora_rmsnorm_fwd(const void* x, int64_t rows, int64_t hidden, int64_t strid
   return cuda_status(mlora::launch_rmsnorm(a, dtype, (cudaStream_t)stream, pdl_on()), "rmsnorm launch");
 }
 
+int mlora_fused_add_rmsnorm_fwd(const void* x, int64_t x_row_stride, void* residual, int64_t residual_row_stride,
+                                int64_t rows, int64_t hidden, const void* w, int32_t w_dtype, void* y,
+                                int64_t y_row_stride, float eps, int32_t dtype, void* stream) {
+  g_err[0] = 0;
+  const int es = elem_size(dtype);
+  if (es == 0) return fail(MLORA_ERR_UNSUPPORTED_DTYPE, "unsupported dtype code %d", dtype);
+  if (elem_size(w_dtype) == 0) return fail(MLORA_ERR_UNSUPPORTED_DTYPE, "unsupported weight dtype %d", w_dtype);
+  if (hidden <= 0 || hidden > INT32_MAX) return fail(MLORA_ERR_INVALID_ARGUMENT, "hidden %lld invalid", (long long)hidden);
+  if (rows < 0) return fail(MLORA_ERR_INVALID_ARGUMENT, "rows < 0");
+  if (x_row_stride < hidden || residual_row_stride < hidden || y_row_stride < hidden)
+    return fail(MLORA_ERR_INVALID_ARGUMENT, "a row stride is smaller than hidden");
+  if (rows == 0) return MLORA_OK;
+  if (x == nullptr || residual == nullptr || w == nullptr || y == nullptr)
+    return fail(MLORA_ERR_INVALID_ARGUMENT, "x / residual / w / y is NULL");
+  mlora::RmsNormArgs a{};
+  a.x = residual;  // rows read, summed with x, written back, normalised
+  a.stride_outer = residual_row_stride;
+  a.stride_inner = 0;
+  a.inner = 1;
+  a.add = x;
+  a.add_stride = x_row_stride;
+  a.res = residual;
+  a.res_stride = residual_row_stride;
+  a.w = w;
+  a.w_dtype = w_dtype;
+  a.y = y;
+  a.y_stride = y_row_stride;
+  a.rows = rows;
+  a.hidden = (int)hidden;
+  a.eps = eps;
+  const int V = 16 / es;
+  a.vec_ok = (hidden % V == 0) && (x_row_stride % V == 0) && (residual_row_stride % V == 0) &&
+             (y_row_stride % V == 0) && aligned(x, 16) && aligned(residual, 16) && aligned(y, 16);
+  return cuda_status(mlora::launch_rmsnorm(a, dtype, (cudaStream_t)stream, pdl_on()), "fused add + rmsnorm launch");
+}
+
 int mlora_scatter_stage(const void* stage, int64_t stage_row_elems, int32_t h, const int64_t* slots,
                         const mlora_scatter_rect_t* rects, int32_t n_rects, int64_t max_rect_elems,
                         int32_t dtype, uint32_t* status, void* stream) {

@@ -59,6 +59,12 @@ struct RmsNormArgs {
   int hidden;
   float eps;
   int vec_ok;
+  // fused add (optional): row r of x is first replaced by T(x[r] + add[r]),
+  // written to res + r * res_stride, and that rounded sum is normalised
+  const void* add;        // nullptr: plain RMSNorm
+  int64_t add_stride;
+  void* res;
+  int64_t res_stride;
 };
 
 // One projection of a fused apply_lora launch; up to kMaxFusedModules

@@ -6,10 +6,41 @@
 // place. A group of G threads owns one row; each thread keeps its CPT chunks of
 // the row in registers, so x is read from HBM exactly once. The norm weight is
 // loaded before griddepcontrol.wait (it is constant for the step).
+//
+// Fused add (optional, the residual add in front of a decoder layer's norm):
+// each chunk of the row is replaced by T(x + add) as it is loaded, written back
+// to the residual row, and the rounded sum is what gets normalised; the result
+// is bit-identical to a separate add followed by this RMSNorm, with one read
+// of the row instead of a write and a re-read.
 #include "common.cuh"
 #include "kernels.h"
 
 namespace mlora {
+
+// a = T(a + b), element by element, in the chunk's packed form
+template <typename T, int V>
+__device__ __forceinline__ void add_round(Chunk<T, V>& a, const Chunk<T, V>& b) {
+  float fa[V], fb[V];
+  a.to_f(fa);
+  b.to_f(fb);
+  if constexpr (V * sizeof(T) == 16) {
+    T o[V];
+#pragma unroll
+    for (int e = 0; e < V; ++e) o[e] = Num<T>::from_f(fa[e] + fb[e]);
+    memcpy(&a.u, o, 16);
+  } else {
+    a.v = Num<T>::from_f(fa[0] + fb[0]);
+  }
+}
+
+template <typename T, int V>
+__device__ __forceinline__ void store_chunk(T* p, const Chunk<T, V>& a) {
+  if constexpr (V * sizeof(T) == 16) {
+    *reinterpret_cast<uint4*>(p) = a.u;
+  } else {
+    *p = a.v;
+  }
+}
 
 template <typename T, int V, int NT, int G, int CPT>
 __global__ void __launch_bounds__(NT) rmsnorm_kernel(const RmsNormArgs p) {
@@ -56,6 +87,9 @@ __global__ void __launch_bounds__(NT) rmsnorm_kernel(const RmsNormArgs p) {
   const T* xr = static_cast<const T*>(p.x);
   if (row_ok) xr += (row / p.inner) * p.stride_outer + (row % p.inner) * p.stride_inner;
   T* yr = static_cast<T*>(p.y) + (row_ok ? row * p.y_stride : 0);
+  const bool fused = p.add != nullptr;
+  const T* ar = static_cast<const T*>(p.add) + (fused && row_ok ? row * p.add_stride : 0);
+  T* rr = static_cast<T*>(p.res) + (fused && row_ok ? row * p.res_stride : 0);
 
   Chunk<T, V> xc[CPT];
   float ss = 0.f;
@@ -63,7 +97,17 @@ __global__ void __launch_bounds__(NT) rmsnorm_kernel(const RmsNormArgs p) {
 #pragma unroll
     for (int j = 0; j < CPT; ++j) {
       const int c = blk * BLK + j * G + gt;
-      if (row_ok && c < nchunk) xc[j].ldcg(xr + (int64_t)c * V); else xc[j].zero();
+      if (row_ok && c < nchunk) {
+        xc[j].ldcg(xr + (int64_t)c * V);
+        if (fused) {  // the residual add: T(x + add), kept and written back
+          Chunk<T, V> ac;
+          ac.ldcg(ar + (int64_t)c * V);
+          add_round(xc[j], ac);
+          store_chunk(rr + (int64_t)c * V, xc[j]);
+        }
+      } else {
+        xc[j].zero();
+      }
       float f[V];
       xc[j].to_f(f);
 #pragma unroll
@@ -88,7 +132,7 @@ __global__ void __launch_bounds__(NT) rmsnorm_kernel(const RmsNormArgs p) {
     for (int j = 0; j < CPT; ++j) {
       const int c = blk * BLK + j * G + gt;
       if (c >= nchunk) continue;
-      if (nblk > 1) xc[j].ldcg(xr + (int64_t)c * V);
+      if (nblk > 1) xc[j].ldcg((fused ? rr : xr) + (int64_t)c * V);  // the rounded sum this thread wrote
       float f[V];
       xc[j].to_f(f);
       if constexpr (V * sizeof(T) == 16) {

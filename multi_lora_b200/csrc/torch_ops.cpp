@@ -268,6 +268,30 @@ at::Tensor rmsnorm(const at::Tensor& x, const at::Tensor& weight, double eps) {
   return rmsnorm_out(x, weight, eps, out);
 }
 
+// residual = T(residual + x) in place, out = rmsnorm(residual) (one kernel).
+void fused_add_rmsnorm(const at::Tensor& x, at::Tensor residual, const at::Tensor& weight, double eps,
+                       at::Tensor out) {
+  const at::Device dev = x.device();
+  check_cuda(x, "x", dev);
+  check_cuda(residual, "residual", dev);
+  check_cuda(weight, "weight", dev);
+  check_cuda(out, "out", dev);
+  const int64_t hidden = x.size(-1);
+  TORCH_CHECK(weight.numel() == hidden && weight.is_contiguous(), "mlora: weight must be contiguous [hidden]");
+  TORCH_CHECK(residual.sizes() == x.sizes() && out.sizes() == x.sizes(), "mlora: x, residual and out must match");
+  TORCH_CHECK(residual.scalar_type() == x.scalar_type() && out.scalar_type() == x.scalar_type(),
+              "mlora: x, residual and out must share a dtype");
+  TORCH_CHECK(x.is_contiguous() && residual.is_contiguous() && out.is_contiguous(),
+              "mlora: x, residual and out must be contiguous");
+  const int64_t rows = hidden > 0 ? x.numel() / hidden : 0;
+  const c10::cuda::CUDAGuard guard(dev);
+  const int rc = mlora_fused_add_rmsnorm_fwd(x.data_ptr(), hidden, residual.data_ptr(), hidden, rows, hidden,
+                                             weight.data_ptr(), dt_code(weight.scalar_type()), out.data_ptr(), hidden,
+                                             (float)eps, dt_code(x.scalar_type()),
+                                             at::cuda::getCurrentCUDAStream().stream());
+  check_rc(rc);
+}
+
 // Slot-load scatter (scatter_bank.py:68-93 of the reference): every block of
 // the h staged banks into its slot. `rects` is a CUDA int64 [n, 6] table of
 // mlora_scatter_rect_t rows (src_offset, dst address, slot_stride, rows, cols,
@@ -317,6 +341,7 @@ TORCH_LIBRARY(mlora, m) {
       "Tensor(b!)? mid=None, Tensor(c!)? status=None) -> ()");
   m.def("rmsnorm(Tensor x, Tensor weight, float eps) -> Tensor");
   m.def("rmsnorm_out(Tensor x, Tensor weight, float eps, Tensor(a!) out) -> Tensor(a!)");
+  m.def("fused_add_rmsnorm(Tensor x, Tensor(a!) residual, Tensor weight, float eps, Tensor(b!) out) -> ()");
   m.def("scatter_stage(Tensor stage, Tensor slots, Tensor rects, int max_rect_elems, Tensor(a!)? status=None) -> ()");
 }
 
@@ -328,4 +353,5 @@ TORCH_LIBRARY_IMPL(mlora, CUDA, m) {
   m.impl("rmsnorm", &rmsnorm);
   m.impl("rmsnorm_out", &rmsnorm_out);
   m.impl("scatter_stage", &scatter_stage);
+  m.impl("fused_add_rmsnorm", &fused_add_rmsnorm);
 }

@@ -3,9 +3,10 @@
 Covers the parts of ``multi_lora/manager.py`` that sit on the hot path:
 ``prepare_lora_batch`` (:172-187), ``build_kernel_input_metadata`` (:189-212),
 ``_setup_forward_batch`` (:214-233) and ``forward_with_lora`` (:237-279).
-Loading adapters from PEFT checkpoints (``from_pretrained``) is not part of
-this package: adapters are registered as :class:`AdapterWeights` and the
-target ``nn.Linear`` modules are wrapped with :func:`wrap_linear_modules`.
+Adapters are registered as :class:`AdapterWeights`, or read from PEFT adapter
+directories with :meth:`MultiLoRAManager.load_adapter` (no ``peft`` install
+needed); the target ``nn.Linear`` modules are wrapped with
+:func:`wrap_linear_modules`.
 """
 
 from __future__ import annotations
@@ -83,6 +84,16 @@ class MultiLoRAManager:
             raise ValueError(f"LoRA name already registered: {name}")
         self._weight_store[name] = weights
         self.pool.ensure_buffers(weights)
+
+    def load_adapter(self, name: str, path, *, dtype: Optional[torch.dtype] = None) -> AdapterWeights:
+        """Register the PEFT adapter saved in directory ``path`` (``adapter_config.json`` +
+        ``adapter_model.safetensors``) under ``name``; no ``peft`` install needed
+        (:func:`multi_lora_b200.peft_io.load_adapter_dir`)."""
+        from multi_lora_b200.peft_io import load_adapter_dir
+
+        weights = load_adapter_dir(path, dtype=dtype)
+        self.register_adapter(name, weights)
+        return weights
 
     def prepare_lora_batch(self, lora_names: List[LoraName]) -> BatchLoRAInfo:
         if not validate_lora_batch(lora_names, max_loras_per_batch=self.max_loras_per_batch):

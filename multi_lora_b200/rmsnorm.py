@@ -25,6 +25,23 @@ def rmsnorm_out(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Te
     return _native.ops().rmsnorm_out(x, weight, float(eps), out)
 
 
+def fused_add_rmsnorm(residual: torch.Tensor, x: torch.Tensor, weight: torch.Tensor, eps: float,
+                      out: torch.Tensor | None = None):
+    """``residual = residual + x`` (in place, rounded to the dtype), then RMSNorm of it.
+
+    The residual add in front of a decoder layer's norm fused with the norm
+    (the reference's planned T22, OPTIMIZATION_TODO.md:125-142). Returns
+    ``(out, residual)``; ``out`` is allocated unless given. Bit-identical to
+    ``residual += x; rmsnorm_fwd(residual, weight, eps)``.
+    """
+    if not (x.is_cuda and residual.is_cuda):
+        raise RuntimeError("mlora: fused_add_rmsnorm needs CUDA tensors (no CPU path)")
+    if out is None:
+        out = torch.empty_like(x, memory_format=torch.contiguous_format)
+    _native.ops().fused_add_rmsnorm(x, residual, weight, float(eps), out)
+    return out, residual
+
+
 def fuse_rmsnorm(model) -> int:
     """Route every ``*RMSNorm`` module with ``variance_epsilon`` through the fused kernel.
 

@@ -114,3 +114,56 @@ def test_fuse_patches_all_and_keeps_numerics(cuda_dev):
 def test_cpu_input_raises():
     with pytest.raises(RuntimeError):
         rmsnorm_fwd(torch.randn(2, 8), torch.ones(8), 1e-6)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("rows, hidden", [(64, 4096), (7, 8192), (5, 1001), (3, 40960)])
+def test_fused_add_rmsnorm_equals_add_then_norm(cuda_dev, dtype, rows, hidden):
+    """residual = T(residual + x), out = rmsnorm(residual): bit-identical to the
+    two-step sequence (a dtype add, then the RMSNorm kernel), and within the
+    kernel's own tolerance of the oracle's RMSNorm of the rounded sum.
+    Shapes: decode rows, rows longer than one register pass (40960), and a
+    hidden size that is not a multiple of the 16-byte chunk (scalar path)."""
+    from multi_lora_b200.rmsnorm import fused_add_rmsnorm
+
+    g = torch.Generator().manual_seed(rows * 131 + hidden)
+    res0 = torch.randn(rows, hidden, generator=g).to(dtype).to(cuda_dev)
+    x = torch.randn(rows, hidden, generator=g).to(dtype).to(cuda_dev)
+    w = (1 + 0.1 * torch.randn(hidden, generator=g)).to(dtype).to(cuda_dev)
+    res = res0.clone()
+    out, res_ret = fused_add_rmsnorm(res, x, w, 1e-6)
+    assert res_ret is res
+    want_res = res0 + x  # torch adds in the dtype (fp32 arithmetic, one rounding)
+    want_out = rmsnorm_fwd(want_res, w, 1e-6)
+    torch.cuda.synchronize()
+    assert torch.equal(res, want_res)
+    assert torch.equal(out, want_out)
+    name = {torch.bfloat16: "bf16", torch.float16: "f16", torch.float32: "f32"}[dtype]
+    oracle_res = O.round_to(C.f32(res0) + C.f32(x), name)
+    np.testing.assert_array_equal(C.f32(res), oracle_res)
+    np.testing.assert_allclose(C.f32(out), O.rmsnorm(oracle_res, C.f32(w), 1e-6, name),
+                               rtol=2 ** -6 if dtype != torch.float32 else 1e-5, atol=1e-5)
+
+
+def test_fused_add_rmsnorm_capi_strided_rows(cuda_dev):
+    """Through the C ABI with row strides wider than hidden (rows inside larger buffers)."""
+    import ctypes
+
+    from multi_lora_b200 import _native
+
+    g = torch.Generator().manual_seed(5)
+    rows, hidden = 6, 512
+    x_big = torch.randn(rows, hidden + 64, generator=g).bfloat16().to(cuda_dev)
+    r_big = torch.randn(rows, hidden + 32, generator=g).bfloat16().to(cuda_dev)
+    y_big = torch.full((rows, hidden + 16), 3.0, dtype=torch.bfloat16, device=cuda_dev)
+    w = torch.randn(hidden, generator=g).bfloat16().to(cuda_dev)
+    x, r, y = x_big[:, :hidden], r_big[:, :hidden], y_big[:, :hidden]
+    want_r = r + x
+    want_y = rmsnorm_fwd(want_r, w, 1e-5)
+    rc = _native.capi().mlora_fused_add_rmsnorm_fwd(
+        x.data_ptr(), x.stride(0), r.data_ptr(), r.stride(0), rows, hidden, w.data_ptr(), 0, y.data_ptr(),
+        y.stride(0), ctypes.c_float(1e-5), 0, torch.cuda.current_stream().cuda_stream)
+    C.check(rc)
+    torch.cuda.synchronize()
+    assert torch.equal(r, want_r) and torch.equal(y, want_y)
+    assert (y_big[:, hidden:] == 3.0).all()  # the row tails are not written
