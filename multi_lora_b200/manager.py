@@ -68,7 +68,9 @@ class MultiLoRAManager:
         max_lora_rank: int = 64,
         eviction_policy: str = "lru",
         lora_backend: str = "cuda",
+        model: Optional[nn.Module] = None,
     ) -> None:
+        self.model = model  # the model whose linears the wrappers sit in (optional)
         self.lora_wrappers = lora_wrappers
         self.max_loras_per_batch = max_loras_per_batch
         self.pool = LoRAMemoryPool(max_loras_per_batch, max_lora_rank, device, dtype, eviction_policy)
@@ -76,6 +78,28 @@ class MultiLoRAManager:
         self._lora_backend: LoRABackend = get_lora_backend(lora_backend)
         self._resident_meta: KernelInputMetaData = empty_kernel_input_metadata(
             device=self.pool.device, dtype=self.pool.dtype)
+
+    @classmethod
+    def from_model(cls, model: nn.Module, *, target_suffixes: Iterable[str], device: torch.device,
+                   dtype: torch.dtype, **kwargs) -> "MultiLoRAManager":
+        """Wrap every ``nn.Linear`` of ``model`` whose name ends with one of
+        ``target_suffixes`` (the reference's ``lora_target_suffixes``,
+        manager.py:94-125) and build a manager that owns ``model``. Keys are the
+        module names normalised like PEFT's (``normalize_module_key``)."""
+        from multi_lora_b200.weights import normalize_module_key
+
+        suffixes = tuple(target_suffixes)
+        names = [n for n, m in model.named_modules() if isinstance(m, nn.Linear) and n.endswith(suffixes)]
+        wrappers = wrap_linear_modules(model, names)
+        keyed = {normalize_module_key(n): w for n, w in wrappers.items()}
+        return cls(keyed, device=device, dtype=dtype, model=model, **kwargs)
+
+    @property
+    def inference_model(self) -> nn.Module:
+        """The model a decode step runs (graph_decode.DecodeStep.run)."""
+        if self.model is None:
+            raise RuntimeError("this manager was built without a model")
+        return self.model
 
     def register_adapter(self, name: str, weights: AdapterWeights) -> None:
         if not name:
@@ -143,9 +167,11 @@ class MultiLoRAManager:
             wrapper.set_lora_info(self._lora_backend, a, b)
 
     @torch.inference_mode()
-    def forward_with_lora(self, model: nn.Module, *, lora_names: List[LoraName], seq_lens: List[int],
-                          x: Optional[torch.Tensor] = None, **kwargs):
-        """Prepare the step, then run ``model(x, **kwargs)`` (or ``model(**kwargs)``)."""
+    def forward_with_lora(self, model: Optional[nn.Module] = None, *, lora_names: List[LoraName],
+                          seq_lens: List[int], x: Optional[torch.Tensor] = None, **kwargs):
+        """Prepare the step, then run ``model(x, **kwargs)`` (or ``model(**kwargs)``);
+        ``model`` defaults to the manager's own."""
+        model = self.inference_model if model is None else model
         self._setup_forward_batch(lora_names, seq_lens=seq_lens)
         with nullcontext():
             if x is not None:
