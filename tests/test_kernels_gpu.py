@@ -113,12 +113,12 @@ def _check_case(c, dev, dtype, scal_dtype=torch.float32):
     # mid: columns >= rank (and whole rank-0 / empty segments) untouched
     m = C.f32(mid_big)
     assert (m[:, R:] == -3.0).all()
+    x32, a32 = C.f32(c["x"]), np.nan_to_num(C.f32(c["A"]))
     for seg, slot in enumerate(c["widx"]):
         r = c["ranks"][slot]
         rows = slice(ind[seg], ind[seg + 1])
         assert (m[rows, r:R] == -3.0).all()
-        mid_want = O.shrink(C.f32(c["x"])[rows], np.nan_to_num(C.f32(c["A"]))[[slot]], [0, rows.stop - rows.start],
-                            [0], [r], 1, "f32")
+        mid_want = O.shrink(x32[rows], a32[[slot]], [0, rows.stop - rows.start], [0], [r], 1, "f32")
         tol_m = 1e-4 if dtype == torch.float32 else 1e-2
         np.testing.assert_allclose(m[rows, :r], mid_want[:, :r], rtol=tol_m, atol=tol_m)
 
@@ -239,11 +239,12 @@ def _check_apply(c, dev, dtype, expect_path=None, force="auto"):
     assert (big[~inner] == 7.0).all()
     m = C.f32(mid_big)
     assert (m[:, R:] == -3.0).all()
+    x32, a32 = C.f32(c["x"]), np.nan_to_num(C.f32(c["A"]))  # once: the stacks can be 100+ MB
     for seg, slot in enumerate(c["widx"]):
         r = c["ranks"][slot]
         rows = slice(ind[seg], ind[seg + 1])
         assert (m[rows, r:R] == -3.0).all()
-        mid_want = C.f32(c["x"])[rows] @ np.nan_to_num(C.f32(c["A"]))[slot, :r].T
+        mid_want = x32[rows] @ a32[slot, :r].T
         np.testing.assert_allclose(m[rows, :r], mid_want, rtol=1e-2, atol=1e-2)
     return path
 
