@@ -177,14 +177,15 @@ def build_workload(wl: Workload, dev, tp_rank: int = 0, tp: int = 1):
     return layers
 
 
-def run_step(wl: Workload, layers, be, parts=("rmsnorm", "lora"), grouped=True, tp=1, tp_rank=0):
+def run_step(wl: Workload, layers, be, parts=("rmsnorm", "lora"), grouped=True, tp=1, tp_rank=0, exchange=None):
     """One forward of the LoRA hot path over all layers, in the model's
     dependency order: rmsnorm -> {q,k,v} -> o -> rmsnorm -> {gate,up} -> down.
 
     grouped: q/k/v and gate/up (shared input) each go through one
     ``apply_lora_group`` call; otherwise one ``apply_lora`` per projection.
     tp > 1: o and down are row-parallel (``row_parallel_apply``: shrink
-    partials, NCCL all-reduce, expand), the rest column-parallel.
+    partials summed over the ranks through ``exchange`` (peer memory) or an
+    NCCL all-reduce, then the expand), the rest column-parallel.
     """
     from multi_lora_b200.rmsnorm import rmsnorm_out
     from multi_lora_b200.tensor_parallel import row_parallel_apply
@@ -199,7 +200,7 @@ def run_step(wl: Workload, layers, be, parts=("rmsnorm", "lora"), grouped=True, 
                 continue
             if tp > 1 and kinds[grp[0]] == ROW:
                 for n in grp:
-                    row_parallel_apply(be, L.x[n], L.A[n], L.B[n], L.y[n], tp_rank, tp)
+                    row_parallel_apply(be, L.x[n], L.A[n], L.B[n], L.y[n], tp_rank, tp, exchange=exchange)
             elif grouped and len(grp) > 1:
                 be.apply_lora_group(L.x[grp[0]], [L.A[n] for n in grp], [L.B[n] for n in grp],
                                     [L.y[n] for n in grp])
@@ -208,7 +209,7 @@ def run_step(wl: Workload, layers, be, parts=("rmsnorm", "lora"), grouped=True, 
                     be.apply_lora(L.x[n], L.A[n], L.B[n], L.y[n])
 
 
-def tp_parity_check(wl: Workload, dev, be, tp_rank: int, tp: int, seed: int = 4242) -> dict:
+def tp_parity_check(wl: Workload, dev, be, tp_rank: int, tp: int, seed: int = 4242, exchange=None) -> dict:
     """One checked layer at N > 1: the tensor-parallel result equals the unsharded one.
 
     Every rank builds the same full-size layer (one seed), computes the
@@ -248,7 +249,7 @@ def tp_parity_check(wl: Workload, dev, be, tp_rank: int, tp: int, seed: int = 42
         else:
             ilo, ihi = shard_bounds(n_in, tp_rank, tp)
             y_part = ybase.clone() if tp_rank == 0 else torch.zeros_like(ybase)
-            row_parallel_apply(be, x[:, ilo:ihi].contiguous(), a_sh, b_sh, y_part, tp_rank, tp)
+            row_parallel_apply(be, x[:, ilo:ihi].contiguous(), a_sh, b_sh, y_part, tp_rank, tp, exchange=exchange)
             dist.all_reduce(y_part)
             got = y_part
         torch.cuda.synchronize()
@@ -611,8 +612,8 @@ def run_pool_workload(args, wl: Workload, dev) -> None:
 def config_block(wl: Workload, n: int) -> dict:
     return {"workload": wl.desc, "global_batch": wl.tokens, "seq_len": 1, "layers": wl.layers,
             "adapters": wl.adapters, "rank": wl.rank,
-            "parallelism": f"tp{n} (q/k/v/gate/up column-parallel, o/down row-parallel + NCCL all-reduce of "
-                           f"fp32 [T, r] partials)" if n > 1 else "single",
+            "parallelism": f"tp{n} (q/k/v/gate/up column-parallel, o/down row-parallel; fp32 [T, r] shrink "
+                           f"partials summed over the ranks)" if n > 1 else "single",
             "l2": "no flush: each step streams the distinct per-layer adapter weights (GBs, > 126 MB L2)"}
 
 
@@ -630,6 +631,9 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--resident-first", action=argparse.BooleanOptionalAction, default=True,
                     help="cfg4: admit tokens whose adapter is resident before the others (fewer loads)")
+    ap.add_argument("--row-exchange", choices=["p2p", "nccl"], default="p2p",
+                    help="N > 1: sum the row-parallel shrink partials through peer memory inside the kernels "
+                         "(p2p) or with an NCCL all-reduce (nccl)")
     ap.add_argument("--ungrouped", action="store_true",
                     help="one apply_lora call per projection instead of grouping q/k/v and gate/up")
     args = ap.parse_args()
@@ -715,8 +719,13 @@ def main() -> None:
     torch.cuda.synchronize()
 
     parity = None
+    exchange = None
+    if world > 1 and args.row_exchange == "p2p":
+        from multi_lora_b200.tensor_parallel import PeerExchange
+
+        exchange = PeerExchange.create(device=dev, max_rows=wl.tokens, max_rank=wl.rank)
     if world > 1:  # one checked layer before anything is timed
-        parity = tp_parity_check(wl, dev, be, rank, tp)
+        parity = tp_parity_check(wl, dev, be, rank, tp, exchange=exchange)
         if parity["parity"] != "ok":
             if rank == 0:
                 print(json.dumps({"metric": METRIC, "error": "tensor-parallel parity mismatch", **parity}),
@@ -727,7 +736,8 @@ def main() -> None:
 
     grouped = not args.ungrouped
     graphs = []
-    step_graph = capture(lambda: run_step(wl, layers, be, grouped=grouped, tp=tp, tp_rank=rank))
+    step_graph = capture(lambda: run_step(wl, layers, be, grouped=grouped, tp=tp, tp_rank=rank,
+                                          exchange=exchange))
     graphs.append(step_graph)
     be.apply_lora(layers[0].x["q"], layers[0].A["q"], layers[0].B["q"], layers[0].y["q"].clone())
     path = _native.capi().mlora_last_apply_path()
@@ -770,7 +780,8 @@ def main() -> None:
     # ---- roofline of the dominant kernel (the apply_lora launches), timed alone ----
     ab = algorithmic_bytes(wl, ids, tp)
     pk = peaks()
-    g_lora = capture(lambda: run_step(wl, layers, be, parts=("lora",), grouped=grouped, tp=tp, tp_rank=rank))
+    g_lora = capture(lambda: run_step(wl, layers, be, parts=("lora",), grouped=grouped, tp=tp, tp_rank=rank,
+                                       exchange=exchange))
     graphs.append(g_lora)
     lora_ms = max_over_ranks(time_graph(g_lora, max(20, args.steps // 4)))
     g_rms = capture(lambda: run_step(wl, layers, be, parts=("rmsnorm",), tp=tp, tp_rank=rank))
@@ -781,7 +792,8 @@ def main() -> None:
     per_launch_ms = lora_ms / lora_launches
     achieved = per_launch_bytes / (per_launch_ms / 1e3) / 1e9
     if tp > 1:
-        kernel = "lora part per rank: apply_fused_kernel (column) + shrink/expand + NCCL all-reduce (row)"
+        kernel = ("lora part per rank: apply_fused_kernel (column) + streaming shrink/expand with the partials "
+                  + ("exchanged over peer memory (row)" if exchange is not None else "NCCL-all-reduced (row)"))
     else:
         kernel = APPLY_KERNELS.get(path, "unknown")
     traffic = read_traffic().get(kernel) if wl.name == "cfg2" and tp == 1 else None
@@ -799,7 +811,7 @@ def main() -> None:
                      "lora_ms_alone": round(lora_ms, 4), "rmsnorm_ms_alone": round(rms_ms, 4),
                      "distinct_adapters": ab["distinct_adapters"], "per_rank": tp > 1}
     if grouped:  # the same work as one apply_lora call per projection, for comparison
-        g_u = capture(lambda: run_step(wl, layers, be, grouped=False, tp=tp, tp_rank=rank))
+        g_u = capture(lambda: run_step(wl, layers, be, grouped=False, tp=tp, tp_rank=rank, exchange=exchange))
         graphs.append(g_u)
         step_roofline["ungrouped_ms_per_step"] = round(max_over_ranks(time_graph(g_u, max(20, args.steps // 4))), 4)
 
@@ -845,6 +857,7 @@ def main() -> None:
         if parity is not None:
             out["parity"] = parity["parity"]
             out["parity_check"] = parity
+            out["row_exchange"] = args.row_exchange
         print(json.dumps(out), flush=True)
     # graphs that hold NCCL calls go before the process group
     del step_graph, g_lora, g_rms
@@ -854,6 +867,8 @@ def main() -> None:
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
+        if exchange is not None:
+            exchange.close()
         torch.distributed.destroy_process_group()
 
 

@@ -215,6 +215,77 @@ int mlora_scatter_stage(const void* stage, int64_t stage_row_elems, int32_t h, c
                         const mlora_scatter_rect_t* rects, int32_t n_rects, int64_t max_rect_elems,
                         int32_t dtype, uint32_t* status, void* stream);
 
+/*
+ * Tensor-parallel row-parallel projections without a separate all-reduce.
+ *
+ * A row-parallel projection (o, down) shards x and A on the input dim; each
+ * rank's shrink gives a partial [rows, rank] that must be summed over the
+ * ranks before the expand (the reference path: NCCL all-reduce of fp32
+ * partials). Here the shrink stores each finished tile of partial rows
+ * straight into every rank's receive buffer over NVLink (plain peer stores)
+ * and raises that tile's flag on every rank (release store, system scope);
+ * the expand waits for the tile's flags from all ranks (bounded wait; on
+ * timeout MLORA_STATUS_TIMEOUT is set and the tile is skipped), sums the
+ * partials in rank order, rounds to `dtype` and adds this rank's output
+ * columns. Flags carry the call's epoch, a counter in each rank's buffer that
+ * the expand advances, so the sequence may be captured in a CUDA graph; every
+ * rank must issue the same calls in the same order.
+ *
+ * Each rank owns one buffer of mlora_peer_exchange_bytes() bytes, made by
+ * mlora_peer_buffer_create (zeroed; its IPC handle is sent to the other ranks,
+ * which map it with mlora_peer_buffer_open). No call here allocates except
+ * mlora_peer_buffer_create. No counterpart in the reference, which has no
+ * tensor parallelism; it takes the place of the NCCL all-reduce of the
+ * row-parallel shrink partials (multi_lora_b200/tensor_parallel.py).
+ */
+#define MLORA_MAX_PEERS 8
+#define MLORA_IPC_HANDLE_BYTES 64
+
+typedef struct mlora_peer_exchange {
+  int32_t tp;         /* ranks in the group, 1..MLORA_MAX_PEERS */
+  int32_t rank;       /* this rank */
+  int32_t max_rows;   /* rows (tokens) a call may have */
+  int32_t max_tiles;  /* tiles a call may have: rows / 8 + adapters used is enough */
+  int32_t max_rank;   /* max_rank of the slot stacks */
+  int32_t reserved;
+  void* buffers[MLORA_MAX_PEERS]; /* rank q's exchange buffer as mapped in this process (buffers[rank]: own) */
+} mlora_peer_exchange_t;
+
+/* Bytes of one rank's exchange buffer: partials [2][tp][max_rows][max_rank]
+ * fp32, flags [tp][max_tiles] uint32, two uint32 counters. */
+size_t mlora_peer_exchange_bytes(int32_t tp, int32_t max_rows, int32_t max_tiles, int32_t max_rank);
+
+/* cudaMalloc + zero a buffer on the current device, and its IPC handle
+ * (MLORA_IPC_HANDLE_BYTES bytes written to ipc_handle). Synchronises the device. */
+int mlora_peer_buffer_create(size_t bytes, void** buffer, void* ipc_handle);
+/* Map another process's buffer from its IPC handle (peer access enabled). */
+int mlora_peer_buffer_open(const void* ipc_handle, void** buffer);
+/* Unmap a buffer opened with mlora_peer_buffer_open. */
+int mlora_peer_buffer_close(void* buffer);
+/* Free a buffer made by mlora_peer_buffer_create. */
+int mlora_peer_buffer_destroy(void* buffer);
+
+/*
+ * One row-parallel projection on this rank: shrink of its input shard with
+ * the partials exchanged as above, then the expand of its output columns.
+ *   x        [rows, in_shard] (row stride x_row_stride), this rank's input columns
+ *   a_shard  [num_slots, max_rank, in_shard]; b_shard [num_slots, out_cols, max_rank]
+ *   y        [rows, out_cols] (row stride y_row_stride): this rank's columns of
+ *            the pre-all-reduce partial output, updated in place
+ * phase: 0 = shrink then expand (normal use); 1 = shrink and publish only;
+ * 2 = wait and expand only. Phases 1 and 2 let one process drive several
+ * ranks' exchanges on ONE GPU (every rank's phase 1 before any rank's phase 2),
+ * so that no kernel ever waits for a kernel queued after it.
+ * Shape range: bf16/f16, in_shard % 16 == 0, max_rank % 8 == 0 and <= 64,
+ * out_cols % 8 == 0, 16-byte aligned operands; otherwise
+ * MLORA_ERR_INVALID_ARGUMENT (use the NCCL path).
+ */
+int mlora_row_parallel_apply_p2p(const void* x, int64_t rows, int64_t in_shard, int64_t x_row_stride,
+                                 const void* a_shard, const void* b_shard, int64_t out_cols, int64_t max_rank,
+                                 const mlora_kernel_input_metadata_t* meta, void* y, int64_t y_row_stride,
+                                 const mlora_peer_exchange_t* xchg, int32_t phase, int32_t dtype, uint32_t* status,
+                                 void* stream);
+
 /* Programmatic dependent launch (on by default; env MLORA_PDL=0 turns it off). */
 void mlora_set_pdl(int enable);
 int mlora_get_pdl(void);

@@ -29,6 +29,20 @@ class NativeLibraryError(RuntimeError):
     """The CUDA extension is missing or failed to load."""
 
 
+class PeerExchangeT(ctypes.Structure):
+    """ctypes mirror of ``mlora_peer_exchange_t``."""
+
+    _fields_ = [
+        ("tp", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("max_rows", ctypes.c_int32),
+        ("max_tiles", ctypes.c_int32),
+        ("max_rank", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+        ("buffers", ctypes.c_void_p * 8),
+    ]
+
+
 class MetadataT(ctypes.Structure):
     """ctypes mirror of ``mlora_kernel_input_metadata_t``."""
 
@@ -67,6 +81,13 @@ CAPI_SIGNATURES = {
     "mlora_fused_add_rmsnorm_fwd": (_I32, [_P, _I64, _P, _I64, _I64, _I64, _P, _I32, _P, _I64, ctypes.c_float,
                                            _I32, _P]),
     "mlora_scatter_stage": (_I32, [_P, _I64, _I32, _P, _P, _I32, _I64, _I32, _P, _P]),
+    "mlora_peer_exchange_bytes": (ctypes.c_size_t, [_I32, _I32, _I32, _I32]),
+    "mlora_peer_buffer_create": (_I32, [ctypes.c_size_t, ctypes.POINTER(_P), _P]),
+    "mlora_peer_buffer_open": (_I32, [_P, ctypes.POINTER(_P)]),
+    "mlora_peer_buffer_close": (_I32, [_P]),
+    "mlora_peer_buffer_destroy": (_I32, [_P]),
+    "mlora_row_parallel_apply_p2p": (_I32, [_P, _I64, _I64, _I64, _P, _P, _I64, _I64, ctypes.POINTER(MetadataT), _P,
+                                            _I64, _P, _I32, _I32, _P, _P]),
     "mlora_set_pdl": (None, [ctypes.c_int]),
     "mlora_get_pdl": (ctypes.c_int, []),
     "mlora_last_error": (ctypes.c_char_p, []),
@@ -151,3 +172,17 @@ def dtype_code(dtype: torch.dtype) -> int:
         return DTYPE_CODE[dtype]
     except KeyError:
         raise TypeError(f"mlora: unsupported dtype {dtype}") from None
+
+
+def meta_struct(meta) -> MetadataT:
+    """``mlora_kernel_input_metadata_t`` for a :class:`KernelInputMetaData` (device int32 tables)."""
+    m = MetadataT()
+    m.bs, m.max_len = int(meta.bs), int(meta.max_len)
+    m.num_slots = int(meta.lora_ranks.numel())
+    m.scalings_dtype = DTYPE_CODE[meta.scalings.dtype]
+    m.seg_lens = meta.seg_lens.data_ptr()
+    m.seg_indptr = meta.seg_indptr.data_ptr()
+    m.weight_indices = meta.weight_indices.data_ptr()
+    m.lora_ranks = meta.lora_ranks.data_ptr()
+    m.scalings = meta.scalings.data_ptr()
+    return m

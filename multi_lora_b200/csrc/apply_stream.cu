@@ -243,11 +243,58 @@ __device__ __forceinline__ StreamModule stream_module(const StreamArgs& p, int m
   return r;
 }
 
+// ---- peer exchange (row-parallel tensor parallelism) ----
+// Flags live in each rank's own memory and are written by every rank over
+// NVLink: a release store at system scope after the partial rows, an acquire
+// load by the reader; a flag carries the epoch of the call (calls completed
+// before it, plus one), so flags only ever increase.
+__device__ __forceinline__ void flag_release_sys(uint32_t* f, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t flag_acquire_sys(const uint32_t* f) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+  return v;
+}
+// The call's epoch: read after griddepcontrol.wait, when every earlier call's
+// expand kernel (which advances the counter) has completed.
+__device__ __forceinline__ uint32_t xchg_epoch(const PeerXchg& x) {
+  return *reinterpret_cast<volatile const uint32_t*>(x.ctr);
+}
+// Offset (elements) of partial row `row` from rank `from` in a receive buffer.
+__device__ __forceinline__ int64_t xchg_row(const PeerXchg& x, uint32_t epoch, int from, int row, int R) {
+  return ((int64_t)(epoch & 1u) * x.tp * x.rows + (int64_t)from * x.rows + row) * R;
+}
+// Bounded wait until every rank's flag for `tile` in this rank's flag array
+// carries at least `want`. False (status bit set) on timeout.
+__device__ __forceinline__ bool xchg_wait(const PeerXchg& x, int tile, uint32_t want, uint32_t* status) {
+  const uint32_t* f = x.flags[x.rank];
+  const uint64_t t0 = global_timer_ns();
+  for (int q = 0; q < x.tp; ++q) {
+    while (flag_acquire_sys(f + (int64_t)q * x.tiles + tile) < want) {
+      if (global_timer_ns() - t0 > kWaitLimitNs) {
+        flag_error(status, kErrTimeout);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+// Counts the expand kernel's finished CTAs; the last one advances the epoch.
+__device__ __forceinline__ void xchg_cta_done(const PeerXchg& x) {
+  __threadfence();
+  if (atomicAdd(&x.ctr[1], 1u) == gridDim.x - 1) {
+    x.ctr[1] = 0u;
+    x.ctr[0] = x.ctr[0] + 1u;
+    __threadfence();
+  }
+}
+
 // ---------------------------------------------------------------------------
 // shrink
 // ---------------------------------------------------------------------------
 template <typename T, int RM>
-__global__ void __launch_bounds__(kStreamThreads, 1) lora_shrink_stream_kernel(const StreamArgs p) {
+__global__ void __launch_bounds__(kStreamThreads, 1) lora_shrink_stream_kernel(const __grid_constant__ StreamArgs p) {
   using SS = ShrinkStage<RM>;
   constexpr int NC = kStreamConsumers, NS = kStreamShrinkStages, TM = kStreamTM, KS = kStreamShrinkSplit;
   constexpr int KC = SS::KC, KCP = SS::KCP;
@@ -268,6 +315,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1) lora_shrink_stream_kernel(c
   const int my_items = cl < n_items ? (n_items - 1 - cl) / NCL + 1 : 0;  // the same for the whole cluster
   if (my_items == 0) {
     pdl_trigger();
+    // exchange: this grid must not complete before the previous call's expand
+    // (it advances the epoch counter the next expand reads)
+    if (p.xchg.tp > 0 && tid == 0) pdl_wait();
     return;
   }
   if (tid == 0) {
@@ -329,6 +379,11 @@ __global__ void __launch_bounds__(kStreamThreads, 1) lora_shrink_stream_kernel(c
     const int g = lane >> 2, cq = lane & 3;
     bool ok = true;
     int f = 0;
+    uint32_t epoch = 0;
+    if (p.xchg.tp > 0) {  // partials go to peers tagged with this call's epoch
+      pdl_wait();
+      epoch = xchg_epoch(p.xchg);
+    }
     const uint32_t recv0 = smem_addr(&s_recv[0][0][0][0]);
     for (int j = 0; j < my_items; ++j) {
       const int item = cl + j * NCL;
@@ -413,18 +468,34 @@ __global__ void __launch_bounds__(kStreamThreads, 1) lora_shrink_stream_kernel(c
         // CTA 0: the KS partials in cluster order, one rounding to T, rows of this tile only
         if (ctid == 0) mbar_arrive_expect_tx(&bar_red[par], (uint32_t)KS * PB);
         if (ok) ok = mbar_wait(&bar_red[par], (j >> 1) & 1, p.status);
-        if (ok) {
+        const int tile = item / p.n_mod;
+        const bool xok = p.xchg.tp == 0 || tile < p.xchg.tiles;
+        if (ok && xok) {
           for (int e = ctid; e < t.nt * t.rank; e += NC * 32) {
             const int r = e / t.rank, k = e - r * t.rank;
             float v = 0.f;
 #pragma unroll
             for (int q = 0; q < KS; ++q) v += s_recv[par][q][r][k];
-            const int64_t at = (int64_t)rt.tok[t.start + r] * p.mid_stride + m * p.R + k;
+            const int row = rt.tok[t.start + r];
+            if (p.xchg.tp > 0) {  // this rank's partial row, into every rank's receive buffer (peer stores)
+              if (row < p.xchg.rows) {
+                const int64_t at = xchg_row(p.xchg, epoch, p.xchg.rank, row, p.R) + k;
+                for (int q = 0; q < p.xchg.tp; ++q) p.xchg.recv[q][at] = v;
+              }
+              continue;
+            }
+            const int64_t at = (int64_t)row * p.mid_stride + m * p.R + k;
             if (p.mid_f32) static_cast<float*>(p.mid)[at] = v;  // a partial, summed across ranks later
             else static_cast<T*>(p.mid)[at] = Num<T>::from_f(v);
           }
         }
-        named_barrier(1, NC * 32);  // done reading s_recv[par]
+        if (!xok && ctid == 0) flag_error(p.status, kErrIndptr);  // more tiles than the exchange holds
+        named_barrier(1, NC * 32);  // done reading s_recv[par]; the partial rows are stored
+        if (p.xchg.tp > 0 && ok && xok && ctid == 0) {  // then the tile's flag on every rank
+          __threadfence_system();
+          for (int q = 0; q < p.xchg.tp; ++q)
+            flag_release_sys(p.xchg.flags[q] + (int64_t)p.xchg.rank * p.xchg.tiles + tile, epoch + 1u);
+        }
         if (ctid > 0 && ctid < KS) {  // release the buffer to the peers for item j + 2
           asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
                            cluster_map(smem_addr(&bar_free[par]), (uint32_t)ctid))
@@ -442,7 +513,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) lora_shrink_stream_kernel(c
 // expand
 // ---------------------------------------------------------------------------
 template <typename T, int RM>
-__global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(const StreamArgs p) {
+__global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(const __grid_constant__ StreamArgs p) {
   using ES = ExpandStage<RM>;
   constexpr int NC = kStreamConsumers, NS = kStreamStages;
   constexpr int OC = ES::OC, OCP = ES::OCP, MP = ES::MP;
@@ -467,6 +538,10 @@ __global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(cons
   const int my_items = blockIdx.x < n_items ? (n_items - 1 - blockIdx.x) / G + 1 : 0;
   if (my_items == 0) {
     pdl_trigger();
+    if (p.xchg.tp > 0 && tid == 0) {
+      pdl_wait();  // the count must follow the earlier calls' increments
+      xchg_cta_done(p.xchg);
+    }
     return;
   }
   if (tid == 0) {
@@ -478,6 +553,7 @@ __global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(cons
   }
   __syncthreads();
   pdl_trigger();
+  const bool xchg = p.xchg.tp > 0;  // mid: the sum of every rank's partials, waited for tile by tile
 
   struct Item {
     StreamTile t;
@@ -509,7 +585,7 @@ __global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(cons
       const Item it = decode(j);
       if (lane == 0) {
         mbar_arrive_expect_tx(&full[s], (uint32_t)(it.ocl * p.R + it.t.nt * it.ocl) * sizeof(T) +
-                                            (uint32_t)it.t.nt * p.R * mid_es);
+                                            (xchg ? 0u : (uint32_t)it.t.nt * p.R * mid_es));
         const T* b = static_cast<const T*>(it.m.b) + ((int64_t)it.t.slot * it.m.out_dim + it.o0) * p.R;
         bulk_copy_g2s(stage_b(s), b, (uint32_t)it.ocl * p.R * sizeof(T), &full[s]);
       }
@@ -523,6 +599,7 @@ __global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(cons
       for (int r = lane; r < 2 * it.t.nt; r += 32) {
         const int t = r >> 1;
         const int64_t row = rt.tok[it.t.start + t];
+        if ((r & 1) != 0 && xchg) continue;  // mid comes from the peers' partials, read by the consumers
         if ((r & 1) == 0) bulk_copy_g2s(stage_y(s) + t * OCP, y + row * it.m.y_stride, it.ocl * sizeof(T), &full[s]);
         else if (p.mid_f32)  // fp32 rows (MP floats apart in the stage)
           bulk_copy_g2s(reinterpret_cast<float*>(stage_m(s)) + t * MP,
@@ -546,21 +623,65 @@ __global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(cons
   const int g = lane >> 2, cq = lane & 3;
   const int brow = lane & 7, bhalf = (lane >> 3) & 1;
   bool ok = true;
+  uint32_t epoch = 0;
+  if (xchg) {
+    pdl_wait();
+    epoch = xchg_epoch(p.xchg);
+  }
+  int waited_tile = -1;
+  bool xgood = true;  // exchange: every rank's partials arrived (on a timeout the stages are still drained)
   for (int j = 0; j < my_items; ++j) {
     const int s = j % NS;
     const Item it = decode(j);
     if (ok) ok = mbar_wait(&full[s], (j / NS) & 1, p.status);  // after a timeout: no more waits
     const int rank = it.t.rank, nt = it.t.nt;
-    if (ok) {
+    if (xchg) {
+      const int tile = (blockIdx.x + j * G) / per_tile;
+      if (tile != waited_tile) {  // every rank's partial rows of this tile have landed here
+        __shared__ int s_xok;
+        if (tid == 0) s_xok = xgood && tile < p.xchg.tiles && xchg_wait(p.xchg, tile, epoch + 1u, p.status);
+        named_barrier(1, NC * 32);
+        xgood = s_xok != 0;
+        waited_tile = tile;
+      }
+    }
+    if (ok && xgood) {
       const float scale = rt.scale[it.t.slot];
       // A operand: the tile's mid rows; columns >= rank (stale in the caller's buffer) are zeroed in registers
       uint32_t am[RM / 16][4];
       const int mrow = (lane & 15) < nt ? (lane & 15) : 0;
       const uint32_t ma = smem_addr(stage_m(s)) + (uint32_t)(mrow * MP + (lane >> 4) * 8) * 2u;
       const float* mf = reinterpret_cast<const float*>(stage_m(s)) + g * MP + 2 * cq;  // fp32 rows (mid_f32)
+      const float* xr = nullptr;  // exchange: this rank's receive buffer, row of token g (from rank 0)
+      if (xchg && g < nt) {
+        const int row = rt.tok[it.t.start + g];
+        xr = row < p.xchg.rows ? p.xchg.recv[p.xchg.rank] + xchg_row(p.xchg, epoch, 0, row, p.R) : nullptr;
+      }
+      const int64_t xq = (int64_t)p.xchg.rows * p.R;  // elements between two ranks' partial rows
 #pragma unroll
       for (int kk = 0; kk < RM / 16; ++kk) {
-        if (p.mid_f32) {  // fragment built from fp32 rows, each pair rounded to T (rows g < nt; g + 8 >= nt)
+        if (xchg) {  // mid = the ranks' partials summed in rank order, each pair rounded to T
+          float2 v0 = make_float2(0.f, 0.f), v2 = v0;
+          const int c0 = kk * 16 + 2 * cq;
+          if (xr != nullptr) {
+            for (int q = 0; q < p.xchg.tp; ++q) {
+              if (c0 < p.R) {
+                const float2 u = __ldcg(reinterpret_cast<const float2*>(xr + q * xq + c0));
+                v0.x += u.x;
+                v0.y += u.y;
+              }
+              if (c0 + 8 < p.R) {
+                const float2 u = __ldcg(reinterpret_cast<const float2*>(xr + q * xq + c0 + 8));
+                v2.x += u.x;
+                v2.y += u.y;
+              }
+            }
+          }
+          am[kk][0] = pack_round2<T>(v0.x, v0.y);
+          am[kk][1] = 0u;
+          am[kk][2] = pack_round2<T>(v2.x, v2.y);
+          am[kk][3] = 0u;
+        } else if (p.mid_f32) {  // fragment built from fp32 rows, each pair rounded to T (rows g < nt; g + 8 >= nt)
           float2 v0 = make_float2(0.f, 0.f), v2 = v0;
           if (g < nt) {
             v0 = *reinterpret_cast<const float2*>(mf + kk * 16);
@@ -661,7 +782,7 @@ __global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(cons
     fence_proxy_async_smem();  // the y tile written above is read next by the bulk stores
     named_barrier(1, NC * 32);
     if (tid == 0) {
-      if (ok) {
+      if (ok && xgood) {
         T* y = static_cast<T*>(it.m.y) + it.o0;
         for (int r = 0; r < nt; ++r)
           bulk_copy_s2g(y + (int64_t)rt.tok[it.t.start + r] * it.m.y_stride, stage_y(s) + r * OCP,
@@ -673,7 +794,10 @@ __global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(cons
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
   }
-  if (tid == 0) bulk_wait_all();
+  if (tid == 0) {
+    bulk_wait_all();
+    if (xchg) xchg_cta_done(p.xchg);
+  }
 }
 
 // ---------------------------------------------------------------------------

@@ -102,6 +102,16 @@ cudaError_t launch_apply_fused(FusedArgs a, int dtype, cudaStream_t st, bool pdl
 
 // Streaming apply (persistent shrink + expand kernels, csrc/apply_stream.cu).
 constexpr int kMaxStreamModules = 4;
+
+// Tensor-parallel exchange of row-parallel shrink partials over peer memory
+// (the layout of mlora_peer_exchange_t, include/mlora_b200.h). tp == 0: off.
+constexpr int kMaxPeers = 8;
+struct PeerXchg {
+  float* recv[kMaxPeers];      // rank q's partials [2][tp][rows][R] fp32, mapped in this process
+  uint32_t* flags[kMaxPeers];  // rank q's flags [tp][tiles], mapped in this process
+  uint32_t* ctr;               // this rank's counters: [0] calls completed (the epoch), [1] finished expand CTAs
+  int tp, rank, rows, tiles;
+};
 struct StreamModule {
   const void* a;          // A stack [K, R, in], contiguous
   const void* b;          // B stack [K, out, R], contiguous
@@ -125,6 +135,7 @@ struct StreamArgs {
   uint32_t* status;
   int phase;              // 0: shrink then expand; 1: shrink only; 2: expand only
   int mid_f32;            // 1: mid holds fp32 (the shrink writes unrounded sums, the expand rounds them to T)
+  PeerXchg xchg;          // tp > 0: partials go to every rank's buffer, the expand sums all ranks' (not `mid`)
 };
 cudaError_t launch_apply_stream(const StreamArgs& a, int dtype, cudaStream_t st, bool pdl);
 

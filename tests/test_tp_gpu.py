@@ -4,7 +4,12 @@
   ranks' fp32 partials), checked against the oracle's fp32 delta and, for
   column-parallel projections, against the unsharded kernel;
 * two or more GPUs: one process per GPU over NCCL through
-  ``row_parallel_apply`` (skipped when the box has one GPU).
+  ``row_parallel_apply`` (skipped when the box has one GPU), with the
+  partials summed by an NCCL all-reduce and by the peer-memory exchange;
+* the peer-memory exchange with 2 and 4 ranks emulated on one GPU (every
+  rank's shrink-and-publish phase, then every rank's wait-and-expand phase, so
+  no kernel waits for one queued after it), repeated calls, inside a CUDA
+  graph, and the bounded wait running out on a flag that nothing sets.
 
 Tolerance: bf16 within atol 2e-2 / rtol 1e-2 of the fp32-accumulated
 reference (the parity bar for bf16 outputs).
@@ -23,7 +28,8 @@ import torch.multiprocessing as mp
 
 from multi_lora_b200.backend import CudaLoRABackend
 from multi_lora_b200.batch_info import KernelInputMetaData
-from multi_lora_b200.tensor_parallel import COLUMN, ROW, row_parallel_apply, shard_bounds, shard_lora_stacks
+from multi_lora_b200.tensor_parallel import (COLUMN, ROW, PeerExchange, row_parallel_apply, row_parallel_apply_p2p,
+                                             shard_bounds, shard_lora_stacks)
 from oracle import lora_oracle as orc
 
 pytestmark = pytest.mark.gpu
@@ -105,6 +111,107 @@ def test_tp_emulated_one_gpu(cuda_dev, tp):
     be.check_routing()
 
 
+def _p2p_setup(dev, tp, c):
+    meta = _meta(c, dev)
+    bes = []
+    for _ in range(tp):
+        be = CudaLoRABackend()
+        be.set_kernel_input_metadata(meta)
+        bes.append(be)
+    x, A, B = c["x"].to(dev), c["A"].to(dev), c["B"].to(dev)
+    ranks = []
+    for p in range(tp):
+        a_s, b_s = shard_lora_stacks(A, B, ROW, p, tp)
+        ilo, ihi = shard_bounds(x.shape[1], p, tp)
+        lo, hi = shard_bounds(B.shape[1], p, tp)
+        ranks.append((x[:, ilo:ihi].contiguous(), a_s, b_s, lo, hi))
+    return bes, ranks
+
+
+def _p2p_call(bes, ranks, xs, y_parts):
+    """All ranks' shrink-and-publish phase, then all ranks' wait-and-expand phase."""
+    for phase in (1, 2):
+        for p, (xp, a_s, b_s, lo, hi) in enumerate(ranks):
+            row_parallel_apply_p2p(bes[p], xp, a_s, b_s, y_parts[p][:, lo:hi], xs[p], phase=phase)
+
+
+@pytest.mark.parametrize("tp", [2, 4])
+def test_p2p_exchange_emulated_one_gpu(cuda_dev, tp):
+    """Sum over ranks of the pre-all-reduce outputs = the unsharded delta; three
+    calls in a row (epochs 1..3, both halves of the double-buffered partials)."""
+    dev = cuda_dev
+    c = _case(seed=5)
+    bes, ranks = _p2p_setup(dev, tp, c)
+    xs = PeerExchange.local_group(tp, device=dev, max_rows=64, max_rank=16)
+    ref = torch.from_numpy(_ref_delta(c))
+    try:
+        for _ in range(3):
+            y_parts = [torch.zeros(c["y"].shape, dtype=torch.bfloat16, device=dev) for _ in range(tp)]
+            _p2p_call(bes, ranks, xs, y_parts)
+            torch.cuda.synchronize()
+            for p, (_, _, _, lo, hi) in enumerate(ranks):  # each rank wrote only its columns
+                assert (y_parts[p][:, :lo] == 0).all() and (y_parts[p][:, hi:] == 0).all()
+            delta = torch.stack([y.float() for y in y_parts]).sum(0).cpu()
+            torch.testing.assert_close(delta, ref, **TOL)
+        for be in bes:
+            be.check_routing()
+    finally:
+        xs[0].close()
+
+
+def test_p2p_exchange_in_cuda_graph(cuda_dev):
+    """The exchange captured once and replayed: the epoch advances on the device."""
+    dev = cuda_dev
+    c = _case(seed=6)
+    tp = 2
+    bes, ranks = _p2p_setup(dev, tp, c)
+    xs = PeerExchange.local_group(tp, device=dev, max_rows=64, max_rank=16)
+    ref = torch.from_numpy(_ref_delta(c))
+    y_parts = [torch.zeros(c["y"].shape, dtype=torch.bfloat16, device=dev) for _ in range(tp)]
+    try:
+        _p2p_call(bes, ranks, xs, y_parts)  # eager once (epoch 1)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for y in y_parts:
+                y.zero_()
+            _p2p_call(bes, ranks, xs, y_parts)
+        for _ in range(3):
+            g.replay()
+            torch.cuda.synchronize()
+            delta = torch.stack([y.float() for y in y_parts]).sum(0).cpu()
+            torch.testing.assert_close(delta, ref, **TOL)
+        for be in bes:
+            be.check_routing()
+        del g
+    finally:
+        xs[0].close()
+
+
+def test_p2p_exchange_wait_times_out_and_reports(cuda_dev):
+    """A rank whose peer never publishes: its bounded wait runs out (about 2 s),
+    the status word carries the timeout bit, the tile is skipped, the context
+    stays usable."""
+    dev = cuda_dev
+    c = _case(seed=7)
+    bes, ranks = _p2p_setup(dev, 2, c)
+    xs = PeerExchange.local_group(2, device=dev, max_rows=64, max_rank=16)
+    try:
+        y = torch.zeros(c["y"].shape, dtype=torch.bfloat16, device=dev)
+        xp, a_s, b_s, lo, hi = ranks[0]
+        row_parallel_apply_p2p(bes[0], xp, a_s, b_s, y[:, lo:hi], xs[0], phase=1)
+        row_parallel_apply_p2p(bes[0], xp, a_s, b_s, y[:, lo:hi], xs[0], phase=2)  # rank 1 never published
+        torch.cuda.synchronize()
+        assert int(bes[0].status_word(dev).item()) & 0x10
+        assert (y == 0).all()  # nothing expanded from a missing partial
+        with pytest.raises(RuntimeError, match="did not complete in time"):
+            bes[0].check_routing()
+        z = torch.ones(4, device=dev) * 2  # the context still runs work
+        assert float(z.sum()) == 8.0
+    finally:
+        xs[0].close()
+
+
 def test_shrink_partial_zero_outside_adapter_columns(cuda_dev):
     """fp32 partials are zero past each slot's rank and on base (rank-0) rows,
     so the all-reduce adds nothing stale."""
@@ -127,7 +234,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _nccl_worker(rank, world, port, q):
+def _nccl_worker(rank, world, port, q, exchange=False):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     torch.cuda.set_device(rank)
@@ -141,10 +248,15 @@ def _nccl_worker(rank, world, port, q):
         a_s, b_s = shard_lora_stacks(A, B, ROW, rank, world)
         ilo, ihi = shard_bounds(x.shape[1], rank, world)
         y_part = torch.zeros(c["y"].shape, dtype=torch.bfloat16, device=dev)
-        for _ in range(2):  # twice: the resident partial buffer is reused
+        xchg = PeerExchange.create(device=dev, max_rows=64, max_rank=16) if exchange else None
+        for _ in range(3):  # repeated: the resident partial buffer (or the exchange's halves) is reused
             y_part.zero_()
-            row_parallel_apply(be, x[:, ilo:ihi].contiguous(), a_s, b_s, y_part, rank, world)
+            row_parallel_apply(be, x[:, ilo:ihi].contiguous(), a_s, b_s, y_part, rank, world, exchange=xchg)
+        torch.cuda.synchronize()
         be.check_routing()
+        if xchg is not None:
+            dist.barrier()
+            xchg.close()
         d = y_part.float()
         dist.all_reduce(d)
         torch.cuda.synchronize()
@@ -155,12 +267,13 @@ def _nccl_worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tp_nccl_row_parallel():
+@pytest.mark.parametrize("exchange", [False, True], ids=["nccl_allreduce", "peer_exchange"])
+def test_tp_nccl_row_parallel(exchange):
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_nccl_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_nccl_worker, args=(r, world, port, q, exchange)) for r in range(world)]
     for p in procs:
         p.start()
     try:
