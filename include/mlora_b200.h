@@ -220,16 +220,16 @@ int mlora_scatter_stage(const void* stage, int64_t stage_row_elems, int32_t h, c
  *
  * A row-parallel projection (o, down) shards x and A on the input dim; each
  * rank's shrink gives a partial [rows, rank] that must be summed over the
- * ranks before the expand (the reference path: NCCL all-reduce of fp32
- * partials). Here the shrink stores each finished tile of partial rows
- * straight into every rank's receive buffer over NVLink (plain peer stores)
- * and raises that tile's flag on every rank (release store, system scope);
- * the expand waits for the tile's flags from all ranks (bounded wait; on
- * timeout MLORA_STATUS_TIMEOUT is set and the tile is skipped), sums the
+ * ranks before the expand (the baseline: an NCCL all-reduce of fp32
+ * partials). Here the shrink stores each partial value straight into every
+ * rank's receive buffer over NVLink (plain peer stores), as one 8-byte word
+ * holding the fp32 value and the call's tag; the expand polls the words it
+ * needs until they carry this call's tag (bounded; on timeout
+ * MLORA_STATUS_TIMEOUT is set and the item is skipped), sums the ranks'
  * partials in rank order, rounds to `dtype` and adds this rank's output
- * columns. Flags carry the call's epoch, a counter in each rank's buffer that
- * the expand advances, so the sequence may be captured in a CUDA graph; every
- * rank must issue the same calls in the same order.
+ * columns. The tag comes from a counter in each rank's buffer that the expand
+ * advances (calls completed), so the calls may be captured in a CUDA graph;
+ * every rank must issue the same calls in the same order.
  *
  * Each rank owns one buffer of mlora_peer_exchange_bytes() bytes, made by
  * mlora_peer_buffer_create (zeroed; its IPC handle is sent to the other ranks,
@@ -242,18 +242,17 @@ int mlora_scatter_stage(const void* stage, int64_t stage_row_elems, int32_t h, c
 #define MLORA_IPC_HANDLE_BYTES 64
 
 typedef struct mlora_peer_exchange {
-  int32_t tp;         /* ranks in the group, 1..MLORA_MAX_PEERS */
-  int32_t rank;       /* this rank */
-  int32_t max_rows;   /* rows (tokens) a call may have */
-  int32_t max_tiles;  /* tiles a call may have: rows / 8 + adapters used is enough */
-  int32_t max_rank;   /* max_rank of the slot stacks */
-  int32_t reserved;
+  int32_t tp;        /* ranks in the group, 1..MLORA_MAX_PEERS */
+  int32_t rank;      /* this rank */
+  int32_t max_rows;  /* rows (tokens) a call may have */
+  int32_t max_rank;  /* max_rank of the slot stacks */
   void* buffers[MLORA_MAX_PEERS]; /* rank q's exchange buffer as mapped in this process (buffers[rank]: own) */
 } mlora_peer_exchange_t;
 
-/* Bytes of one rank's exchange buffer: partials [2][tp][max_rows][max_rank]
- * fp32, flags [tp][max_tiles] uint32, two uint32 counters. */
-size_t mlora_peer_exchange_bytes(int32_t tp, int32_t max_rows, int32_t max_tiles, int32_t max_rank);
+/* Bytes of one rank's exchange buffer: tagged partial words
+ * [2][tp][max_rows][max_rank] of 8 bytes (two halves alternate between
+ * calls) and two uint32 counters. */
+size_t mlora_peer_exchange_bytes(int32_t tp, int32_t max_rows, int32_t max_rank);
 
 /* cudaMalloc + zero a buffer on the current device, and its IPC handle
  * (MLORA_IPC_HANDLE_BYTES bytes written to ipc_handle). Synchronises the device. */

@@ -36,9 +36,7 @@ class PeerExchangeT(ctypes.Structure):
         ("tp", ctypes.c_int32),
         ("rank", ctypes.c_int32),
         ("max_rows", ctypes.c_int32),
-        ("max_tiles", ctypes.c_int32),
         ("max_rank", ctypes.c_int32),
-        ("reserved", ctypes.c_int32),
         ("buffers", ctypes.c_void_p * 8),
     ]
 
@@ -81,7 +79,7 @@ CAPI_SIGNATURES = {
     "mlora_fused_add_rmsnorm_fwd": (_I32, [_P, _I64, _P, _I64, _I64, _I64, _P, _I32, _P, _I64, ctypes.c_float,
                                            _I32, _P]),
     "mlora_scatter_stage": (_I32, [_P, _I64, _I32, _P, _P, _I32, _I64, _I32, _P, _P]),
-    "mlora_peer_exchange_bytes": (ctypes.c_size_t, [_I32, _I32, _I32, _I32]),
+    "mlora_peer_exchange_bytes": (ctypes.c_size_t, [_I32, _I32, _I32]),
     "mlora_peer_buffer_create": (_I32, [ctypes.c_size_t, ctypes.POINTER(_P), _P]),
     "mlora_peer_buffer_open": (_I32, [_P, ctypes.POINTER(_P)]),
     "mlora_peer_buffer_close": (_I32, [_P]),

@@ -244,46 +244,51 @@ __device__ __forceinline__ StreamModule stream_module(const StreamArgs& p, int m
 }
 
 // ---- peer exchange (row-parallel tensor parallelism) ----
-// Flags live in each rank's own memory and are written by every rank over
-// NVLink: a release store at system scope after the partial rows, an acquire
-// load by the reader; a flag carries the epoch of the call (calls completed
-// before it, plus one), so flags only ever increase.
-__device__ __forceinline__ void flag_release_sys(uint32_t* f, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
+// Every partial value goes to every rank as one 8-byte word {fp32 bits, tag}
+// with tag = epoch + 1 of the call; the reader polls its words until the tag
+// is this call's. The epoch is the number of calls the expand kernel has
+// completed; the words alternate between two halves by epoch parity, so a
+// rank one call ahead never overwrites words still being read.
+__device__ __forceinline__ void word_store_sys(unsigned long long* w, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(w), "l"(v) : "memory");
 }
-__device__ __forceinline__ uint32_t flag_acquire_sys(const uint32_t* f) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-  return v;
+__device__ __forceinline__ void word_load_pair(const unsigned long long* w, unsigned long long& a,
+                                               unsigned long long& b) {
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(w) : "memory");
 }
 // The call's epoch: read after griddepcontrol.wait, when every earlier call's
 // expand kernel (which advances the counter) has completed.
 __device__ __forceinline__ uint32_t xchg_epoch(const PeerXchg& x) {
   return *reinterpret_cast<volatile const uint32_t*>(x.ctr);
 }
-// Offset (elements) of partial row `row` from rank `from` in a receive buffer.
+// Offset (words) of partial row `row` from rank `from` in a receive buffer.
 __device__ __forceinline__ int64_t xchg_row(const PeerXchg& x, uint32_t epoch, int from, int row, int R) {
   return ((int64_t)(epoch & 1u) * x.tp * x.rows + (int64_t)from * x.rows + row) * R;
 }
-// Bounded wait until every rank's flag for `tile` in this rank's flag array
-// carries at least `want`. False (status bit set) on timeout.
-__device__ __forceinline__ bool xchg_wait(const PeerXchg& x, int tile, uint32_t want, uint32_t* status) {
-  const uint32_t* f = x.flags[x.rank];
-  const uint64_t t0 = global_timer_ns();
-  for (int q = 0; q < x.tp; ++q) {
-    while (flag_acquire_sys(f + (int64_t)q * x.tiles + tile) < want) {
-      if (global_timer_ns() - t0 > kWaitLimitNs) {
-        flag_error(status, kErrTimeout);
-        return false;
-      }
-    }
+// Two adjacent words (columns c, c + 1 of one rank's row), polled until both
+// carry `tag` (each column only if it is below `live`); bounded by
+// kWaitLimitNs from `t0`. Returns false on timeout.
+__device__ __forceinline__ bool poll_pair(const unsigned long long* w, uint32_t tag, int c, int live, float& v0,
+                                          float& v1, uint64_t& t0) {
+  unsigned long long a, b;
+  word_load_pair(w, a, b);
+  const bool need0 = c < live, need1 = c + 1 < live;
+  while ((need0 && (uint32_t)(a >> 32) != tag) || (need1 && (uint32_t)(b >> 32) != tag)) {
+    if (t0 == 0) t0 = global_timer_ns();
+    else if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+    word_load_pair(w, a, b);
   }
+  v0 = need0 ? __uint_as_float((uint32_t)a) : 0.f;
+  v1 = need1 ? __uint_as_float((uint32_t)b) : 0.f;
   return true;
 }
-// Counts the expand kernel's finished CTAs; the last one advances the epoch.
-__device__ __forceinline__ void xchg_cta_done(const PeerXchg& x) {
+// Counts the expand kernel's CTAs that had items (`working` of them); the
+// last one advances the epoch. Only CTAs with items count: each of them read
+// the epoch after its griddepcontrol.wait, and that wait already implies the
+// previous call's expand kernel completed, so two calls never count at once.
+__device__ __forceinline__ void xchg_cta_done(const PeerXchg& x, uint32_t working) {
   __threadfence();
-  if (atomicAdd(&x.ctr[1], 1u) == gridDim.x - 1) {
+  if (atomicAdd(&x.ctr[1], 1u) == working - 1u) {
     x.ctr[1] = 0u;
     x.ctr[0] = x.ctr[0] + 1u;
     __threadfence();
@@ -315,9 +320,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1) lora_shrink_stream_kernel(c
   const int my_items = cl < n_items ? (n_items - 1 - cl) / NCL + 1 : 0;  // the same for the whole cluster
   if (my_items == 0) {
     pdl_trigger();
-    // exchange: this grid must not complete before the previous call's expand
-    // (it advances the epoch counter the next expand reads)
-    if (p.xchg.tp > 0 && tid == 0) pdl_wait();
+    // exchange with nothing to do at all: the grid must still not complete
+    // before the previous call's expand (it advances the epoch the next call reads)
+    if (p.xchg.tp > 0 && n_items == 0 && tid == 0) pdl_wait();
     return;
   }
   if (tid == 0) {
@@ -468,19 +473,18 @@ __global__ void __launch_bounds__(kStreamThreads, 1) lora_shrink_stream_kernel(c
         // CTA 0: the KS partials in cluster order, one rounding to T, rows of this tile only
         if (ctid == 0) mbar_arrive_expect_tx(&bar_red[par], (uint32_t)KS * PB);
         if (ok) ok = mbar_wait(&bar_red[par], (j >> 1) & 1, p.status);
-        const int tile = item / p.n_mod;
-        const bool xok = p.xchg.tp == 0 || tile < p.xchg.tiles;
-        if (ok && xok) {
+        if (ok) {
           for (int e = ctid; e < t.nt * t.rank; e += NC * 32) {
             const int r = e / t.rank, k = e - r * t.rank;
             float v = 0.f;
 #pragma unroll
             for (int q = 0; q < KS; ++q) v += s_recv[par][q][r][k];
             const int row = rt.tok[t.start + r];
-            if (p.xchg.tp > 0) {  // this rank's partial row, into every rank's receive buffer (peer stores)
+            if (p.xchg.tp > 0) {  // this rank's partial value, tagged, into every rank's buffer (peer stores)
               if (row < p.xchg.rows) {
                 const int64_t at = xchg_row(p.xchg, epoch, p.xchg.rank, row, p.R) + k;
-                for (int q = 0; q < p.xchg.tp; ++q) p.xchg.recv[q][at] = v;
+                const unsigned long long w = ((unsigned long long)(epoch + 1u) << 32) | __float_as_uint(v);
+                for (int q = 0; q < p.xchg.tp; ++q) word_store_sys(p.xchg.recv[q] + at, w);
               }
               continue;
             }
@@ -489,13 +493,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) lora_shrink_stream_kernel(c
             else static_cast<T*>(p.mid)[at] = Num<T>::from_f(v);
           }
         }
-        if (!xok && ctid == 0) flag_error(p.status, kErrIndptr);  // more tiles than the exchange holds
-        named_barrier(1, NC * 32);  // done reading s_recv[par]; the partial rows are stored
-        if (p.xchg.tp > 0 && ok && xok && ctid == 0) {  // then the tile's flag on every rank
-          __threadfence_system();
-          for (int q = 0; q < p.xchg.tp; ++q)
-            flag_release_sys(p.xchg.flags[q] + (int64_t)p.xchg.rank * p.xchg.tiles + tile, epoch + 1u);
-        }
+        named_barrier(1, NC * 32);  // done reading s_recv[par]
         if (ctid > 0 && ctid < KS) {  // release the buffer to the peers for item j + 2
           asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
                            cluster_map(smem_addr(&bar_free[par]), (uint32_t)ctid))
@@ -538,10 +536,7 @@ __global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(cons
   const int my_items = blockIdx.x < n_items ? (n_items - 1 - blockIdx.x) / G + 1 : 0;
   if (my_items == 0) {
     pdl_trigger();
-    if (p.xchg.tp > 0 && tid == 0) {
-      pdl_wait();  // the count must follow the earlier calls' increments
-      xchg_cta_done(p.xchg);
-    }
+    if (p.xchg.tp > 0 && n_items == 0 && tid == 0) pdl_wait();  // as in the shrink: keep the call order
     return;
   }
   if (tid == 0) {
@@ -628,52 +623,50 @@ __global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(cons
     pdl_wait();
     epoch = xchg_epoch(p.xchg);
   }
-  int waited_tile = -1;
-  bool xgood = true;  // exchange: every rank's partials arrived (on a timeout the stages are still drained)
+  __shared__ int s_xfail;  // exchange: a lane's poll ran out (the item is skipped, stages still drained)
+  if (tid == 0) s_xfail = 0;
+  named_barrier(1, NC * 32);
+  bool xgood = true;
   for (int j = 0; j < my_items; ++j) {
     const int s = j % NS;
     const Item it = decode(j);
     if (ok) ok = mbar_wait(&full[s], (j / NS) & 1, p.status);  // after a timeout: no more waits
     const int rank = it.t.rank, nt = it.t.nt;
-    if (xchg) {
-      const int tile = (blockIdx.x + j * G) / per_tile;
-      if (tile != waited_tile) {  // every rank's partial rows of this tile have landed here
-        __shared__ int s_xok;
-        if (tid == 0) s_xok = xgood && tile < p.xchg.tiles && xchg_wait(p.xchg, tile, epoch + 1u, p.status);
-        named_barrier(1, NC * 32);
-        xgood = s_xok != 0;
-        waited_tile = tile;
-      }
-    }
-    if (ok && xgood) {
+    {
+      // ok differs between threads only after a copy-wait timeout; every barrier below is reached by all
+      const bool run = ok && xgood;
       const float scale = rt.scale[it.t.slot];
       // A operand: the tile's mid rows; columns >= rank (stale in the caller's buffer) are zeroed in registers
       uint32_t am[RM / 16][4];
       const int mrow = (lane & 15) < nt ? (lane & 15) : 0;
       const uint32_t ma = smem_addr(stage_m(s)) + (uint32_t)(mrow * MP + (lane >> 4) * 8) * 2u;
       const float* mf = reinterpret_cast<const float*>(stage_m(s)) + g * MP + 2 * cq;  // fp32 rows (mid_f32)
-      const float* xr = nullptr;  // exchange: this rank's receive buffer, row of token g (from rank 0)
+      const unsigned long long* xr = nullptr;  // exchange: this rank's buffer, row of token g (from rank 0)
       if (xchg && g < nt) {
         const int row = rt.tok[it.t.start + g];
         xr = row < p.xchg.rows ? p.xchg.recv[p.xchg.rank] + xchg_row(p.xchg, epoch, 0, row, p.R) : nullptr;
       }
-      const int64_t xq = (int64_t)p.xchg.rows * p.R;  // elements between two ranks' partial rows
+      const int64_t xq = (int64_t)p.xchg.rows * p.R;  // words between two ranks' partial rows
+      const uint32_t tag = epoch + 1u;
+      uint64_t t0 = 0;
+      bool lane_ok = true;
 #pragma unroll
       for (int kk = 0; kk < RM / 16; ++kk) {
-        if (xchg) {  // mid = the ranks' partials summed in rank order, each pair rounded to T
+        if (xchg) {  // mid = the ranks' partials (polled until tagged with this call) in rank order, rounded to T
           float2 v0 = make_float2(0.f, 0.f), v2 = v0;
           const int c0 = kk * 16 + 2 * cq;
-          if (xr != nullptr) {
-            for (int q = 0; q < p.xchg.tp; ++q) {
-              if (c0 < p.R) {
-                const float2 u = __ldcg(reinterpret_cast<const float2*>(xr + q * xq + c0));
-                v0.x += u.x;
-                v0.y += u.y;
+          if (xr != nullptr && run) {
+            for (int q = 0; q < p.xchg.tp && lane_ok; ++q) {
+              float a, b;
+              if (c0 < rank) {
+                lane_ok = poll_pair(xr + q * xq + c0, tag, c0, rank, a, b, t0);
+                v0.x += a;
+                v0.y += b;
               }
-              if (c0 + 8 < p.R) {
-                const float2 u = __ldcg(reinterpret_cast<const float2*>(xr + q * xq + c0 + 8));
-                v2.x += u.x;
-                v2.y += u.y;
+              if (c0 + 8 < rank && lane_ok) {
+                lane_ok = poll_pair(xr + q * xq + c0 + 8, tag, c0 + 8, rank, a, b, t0);
+                v2.x += a;
+                v2.y += b;
               }
             }
           }
@@ -702,6 +695,15 @@ __global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(cons
         am[kk][2] &= m1;
         am[kk][3] &= m1;
       }
+      if (xchg) {  // every lane's partials arrived, or the item is skipped (and reported): all consumers vote
+        if (!lane_ok) {
+          s_xfail = 1;
+          flag_error(p.status, kErrTimeout);
+        }
+        named_barrier(1, NC * 32);
+        xgood = s_xfail == 0;
+      }
+      const bool compute = run && xgood;
       const int ksteps = (rank + 15) / 16;
       const uint32_t ba = smem_addr(stage_b(s));
       T* ys = stage_y(s);
@@ -728,7 +730,7 @@ __global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(cons
           *yp = pack_round2<T>(Pack2<T>::lo(d) + Pack2<T>::lo(u), Pack2<T>::hi(d) + Pack2<T>::hi(u));
         }
       };
-      const int ntl = it.ocl / 8;
+      const int ntl = compute ? it.ocl / 8 : 0;  // nothing written for a skipped item
       if (rank % 16 == 0) {
         // Whole 16-column k-steps (every rank column is valid, no masks): the
         // loop is issue-bound, so its addresses advance by fixed strides with
@@ -796,7 +798,7 @@ __global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(cons
   }
   if (tid == 0) {
     bulk_wait_all();
-    if (xchg) xchg_cta_done(p.xchg);
+    if (xchg) xchg_cta_done(p.xchg, (uint32_t)min(G, n_items));
   }
 }
 

@@ -104,13 +104,15 @@ cudaError_t launch_apply_fused(FusedArgs a, int dtype, cudaStream_t st, bool pdl
 constexpr int kMaxStreamModules = 4;
 
 // Tensor-parallel exchange of row-parallel shrink partials over peer memory
-// (the layout of mlora_peer_exchange_t, include/mlora_b200.h). tp == 0: off.
+// (buffers of mlora_peer_exchange_t, include/mlora_b200.h). tp == 0: off.
+// A partial value travels in one 8-byte word: the fp32 bits in the low half,
+// the call's tag (epoch + 1) in the high half, written and read as one
+// single-copy-atomic 8-byte access, so the reader needs no separate flag.
 constexpr int kMaxPeers = 8;
 struct PeerXchg {
-  float* recv[kMaxPeers];      // rank q's partials [2][tp][rows][R] fp32, mapped in this process
-  uint32_t* flags[kMaxPeers];  // rank q's flags [tp][tiles], mapped in this process
-  uint32_t* ctr;               // this rank's counters: [0] calls completed (the epoch), [1] finished expand CTAs
-  int tp, rank, rows, tiles;
+  unsigned long long* recv[kMaxPeers];  // rank q's words [2][tp][rows][R], mapped in this process
+  uint32_t* ctr;                        // this rank's counters: [0] epoch (calls completed), [1] finished expand CTAs
+  int tp, rank, rows;
 };
 struct StreamModule {
   const void* a;          // A stack [K, R, in], contiguous

@@ -17,11 +17,10 @@ int cuda_rc(cudaError_t e) { return e == cudaSuccess ? MLORA_OK : xfail(MLORA_ER
 bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
 
 struct XLayout {
-  size_t recv, flags, ctr, total;
-  XLayout(int tp, int rows, int tiles, int R) {
-    recv = 0;
-    flags = recv + (size_t)2 * tp * rows * R * sizeof(float);
-    ctr = flags + (size_t)tp * tiles * sizeof(uint32_t);
+  size_t recv, ctr, total;
+  XLayout(int tp, int rows, int R) {
+    recv = 0;  // [2][tp][rows][R] words of 8 bytes
+    ctr = recv + (size_t)2 * tp * rows * R * sizeof(unsigned long long);
     total = (ctr + 2 * sizeof(uint32_t) + 255) / 256 * 256;
   }
 };
@@ -30,9 +29,9 @@ struct XLayout {
 
 extern "C" {
 
-size_t mlora_peer_exchange_bytes(int32_t tp, int32_t max_rows, int32_t max_tiles, int32_t max_rank) {
-  if (tp < 1 || tp > MLORA_MAX_PEERS || max_rows < 1 || max_tiles < 1 || max_rank < 1) return 0;
-  return XLayout(tp, max_rows, max_tiles, max_rank).total;
+size_t mlora_peer_exchange_bytes(int32_t tp, int32_t max_rows, int32_t max_rank) {
+  if (tp < 1 || tp > MLORA_MAX_PEERS || max_rows < 1 || max_rank < 1) return 0;
+  return XLayout(tp, max_rows, max_rank).total;
 }
 
 int mlora_peer_buffer_create(size_t bytes, void** buffer, void* ipc_handle) {
@@ -91,7 +90,7 @@ int mlora_row_parallel_apply_p2p(const void* x, int64_t rows, int64_t in_shard, 
     return xfail(MLORA_ERR_INVALID_ARGUMENT, "shape outside the exchange path (use the NCCL path)");
   if (meta->bs == 0 || rows == 0) return MLORA_OK;
 
-  const XLayout L(X.tp, X.max_rows, X.max_tiles, X.max_rank);
+  const XLayout L(X.tp, X.max_rows, X.max_rank);
   mlora::StreamArgs sa{};
   sa.x = x;
   sa.x_stride = x_row_stride;
@@ -119,12 +118,8 @@ int mlora_row_parallel_apply_p2p(const void* x, int64_t rows, int64_t in_shard, 
   sa.xchg.tp = X.tp;
   sa.xchg.rank = X.rank;
   sa.xchg.rows = X.max_rows;
-  sa.xchg.tiles = X.max_tiles;
-  for (int q = 0; q < X.tp; ++q) {
-    unsigned char* b = static_cast<unsigned char*>(X.buffers[q]);
-    sa.xchg.recv[q] = reinterpret_cast<float*>(b + L.recv);
-    sa.xchg.flags[q] = reinterpret_cast<uint32_t*>(b + L.flags);
-  }
+  for (int q = 0; q < X.tp; ++q)
+    sa.xchg.recv[q] = reinterpret_cast<unsigned long long*>(static_cast<unsigned char*>(X.buffers[q]) + L.recv);
   sa.xchg.ctr = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(X.buffers[X.rank]) + L.ctr);
   const cudaError_t e = mlora::launch_apply_stream(sa, dtype, (cudaStream_t)stream, mlora_get_pdl() != 0);
   if (e == cudaErrorNotSupported) return xfail(MLORA_ERR_INVALID_ARGUMENT, "shape outside the exchange path");

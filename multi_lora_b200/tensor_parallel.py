@@ -22,9 +22,10 @@ path shards naturally (Megatron-style column / row parallel projections):
 Only the ``[S, R]`` partials cross NVLink (64 KiB at S=1024, R=16). Two
 ways to sum them: an NCCL all-reduce (the baseline), or a
 :class:`PeerExchange`, where the shrink kernel stores each finished tile of
-partial rows into every rank's buffer over NVLink and the expand kernel waits
-for the tile's flags and sums the ranks' rows itself (no separate
-collective, memset or launch; ``mlora_row_parallel_apply_p2p``).
+partial value into every rank's buffer over NVLink as an 8-byte word tagged
+with the call, and the expand kernel polls the words until they carry the
+call's tag and sums the ranks' values itself (no separate collective, memset
+or launch; ``mlora_row_parallel_apply_p2p``).
 """
 
 from __future__ import annotations
@@ -85,18 +86,17 @@ def column_parallel_apply(backend, x: torch.Tensor, a_stack: torch.Tensor, b_sha
 class PeerExchange:
     """One rank's end of the row-parallel partial exchange over peer memory.
 
-    Every rank owns one zeroed device buffer (partials, per-tile flags, the
-    call counter) made by ``mlora_peer_buffer_create``; the ranks trade CUDA
-    IPC handles and map each other's buffers (:meth:`create`). Every rank must
-    then run the same row-parallel calls in the same order. ``max_rows`` bounds
-    the rows of a call; ``max_tiles`` the tiles of 8 same-adapter rows
-    (``max_rows + max_rows // 8`` always suffices).
+    Every rank owns one zeroed device buffer (tagged partial words, the call
+    counter) made by ``mlora_peer_buffer_create``; the ranks trade CUDA IPC
+    handles and map each other's buffers (:meth:`create`). Every rank must
+    then run the same row-parallel calls in the same order. ``max_rows``
+    bounds the rows of a call.
     """
 
-    def __init__(self, tp: int, rank: int, max_rows: int, max_rank: int, max_tiles: int, buffers: List[int],
-                 owned: bool, opened: List[int]):
+    def __init__(self, tp: int, rank: int, max_rows: int, max_rank: int, buffers: List[int], owned: bool,
+                 opened: List[int]):
         self.tp, self.rank = tp, rank
-        self.max_rows, self.max_rank, self.max_tiles = max_rows, max_rank, max_tiles
+        self.max_rows, self.max_rank = max_rows, max_rank
         self.buffers = list(buffers)
         self._owned = owned
         self._opened = list(opened)
@@ -112,15 +112,14 @@ class PeerExchange:
         return ptr.value, bytes(handle)
 
     @classmethod
-    def create(cls, *, device: torch.device, max_rows: int, max_rank: int, max_tiles: Optional[int] = None,
+    def create(cls, *, device: torch.device, max_rows: int, max_rank: int,
                group: Optional[dist.ProcessGroup] = None) -> "PeerExchange":
         """Collective over ``group``: make this rank's buffer and map every peer's."""
         from multi_lora_b200 import _native
 
         tp, rank = dist.get_world_size(group), dist.get_rank(group)
-        tiles = max_tiles if max_tiles is not None else max_rows + max_rows // 8
         lib = _native.capi()
-        nbytes = lib.mlora_peer_exchange_bytes(tp, max_rows, tiles, max_rank)
+        nbytes = lib.mlora_peer_exchange_bytes(tp, max_rows, max_rank)
         if nbytes == 0:
             raise ValueError(f"exchange sizes out of range (tp={tp}, rows={max_rows}, rank={max_rank})")
         with torch.cuda.device(device):
@@ -137,21 +136,19 @@ class PeerExchange:
                 _native.check(lib.mlora_peer_buffer_open(hb, ctypes.byref(ptr)))
                 bufs.append(ptr.value)
                 opened.append(ptr.value)
-        return cls(tp, rank, max_rows, max_rank, tiles, bufs, True, opened)
+        return cls(tp, rank, max_rows, max_rank, bufs, True, opened)
 
     @classmethod
-    def local_group(cls, tp: int, *, device: torch.device, max_rows: int, max_rank: int,
-                    max_tiles: Optional[int] = None) -> List["PeerExchange"]:
+    def local_group(cls, tp: int, *, device: torch.device, max_rows: int, max_rank: int) -> List["PeerExchange"]:
         """``tp`` ranks' exchanges in one process on one GPU (every buffer local).
         Drive them with phase 1 for every rank, then phase 2 for every rank,
         so that no kernel waits for one queued after it."""
         from multi_lora_b200 import _native
 
-        tiles = max_tiles if max_tiles is not None else max_rows + max_rows // 8
-        nbytes = _native.capi().mlora_peer_exchange_bytes(tp, max_rows, tiles, max_rank)
+        nbytes = _native.capi().mlora_peer_exchange_bytes(tp, max_rows, max_rank)
         with torch.cuda.device(device):
             bufs = [cls._create_buffer(nbytes)[0] for _ in range(tp)]
-        out = [cls(tp, r, max_rows, max_rank, tiles, bufs, False, []) for r in range(tp)]
+        out = [cls(tp, r, max_rows, max_rank, bufs, False, []) for r in range(tp)]
         out[0]._owned_all = bufs  # rank 0's object frees every buffer
         return out
 
@@ -160,8 +157,7 @@ class PeerExchange:
 
         if self._struct is None:
             st = _native.PeerExchangeT()
-            st.tp, st.rank, st.max_rows, st.max_tiles, st.max_rank = (self.tp, self.rank, self.max_rows,
-                                                                       self.max_tiles, self.max_rank)
+            st.tp, st.rank, st.max_rows, st.max_rank = self.tp, self.rank, self.max_rows, self.max_rank
             for q, b in enumerate(self.buffers):
                 st.buffers[q] = b
             self._struct = st

@@ -9,7 +9,7 @@
 * the peer-memory exchange with 2 and 4 ranks emulated on one GPU (every
   rank's shrink-and-publish phase, then every rank's wait-and-expand phase, so
   no kernel waits for one queued after it), repeated calls, inside a CUDA
-  graph, and the bounded wait running out on a flag that nothing sets.
+  graph, and the bounded wait running out on partials that no rank writes.
 
 Tolerance: bf16 within atol 2e-2 / rtol 1e-2 of the fp32-accumulated
 reference (the parity bar for bf16 outputs).
@@ -189,7 +189,7 @@ def test_p2p_exchange_in_cuda_graph(cuda_dev):
 
 
 def test_p2p_exchange_wait_times_out_and_reports(cuda_dev):
-    """A rank whose peer never publishes: its bounded wait runs out (about 2 s),
+    """A rank whose peer never publishes: its bounded polls run out (about 2 s),
     the status word carries the timeout bit, the tile is skipped, the context
     stays usable."""
     dev = cuda_dev
