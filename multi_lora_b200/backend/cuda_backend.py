@@ -3,6 +3,12 @@
 Takes the place of ``TritonLoRABackend`` (multi_lora/backend/triton_backend.py:19-78)
 with the same methods. There is no CPU or Torch fallback: a non-CUDA input or
 a missing extension raises.
+
+The kernels behind these methods allocate nothing; this layer allocates only
+in two cases the normal path never meets: an output whose column stride is
+not 1 goes through a contiguous temporary (copied back), and routing tables
+that are not int32 are converted per call (``write_kernel_input_metadata``
+writes int32).
 """
 
 from __future__ import annotations

@@ -298,8 +298,10 @@ __device__ __forceinline__ void xchg_cta_done(const PeerXchg& x, uint32_t workin
 // ---------------------------------------------------------------------------
 // shrink
 // ---------------------------------------------------------------------------
-template <typename T, int RM>
-__global__ void __launch_bounds__(kStreamThreads, 1) lora_shrink_stream_kernel(const __grid_constant__ StreamArgs p) {
+// XCHG: the row-parallel peer exchange (p.xchg) is on; a separate instance,
+// so the plain kernels carry none of its code.
+template <typename T, int RM, bool XCHG>
+__global__ void __launch_bounds__(kStreamThreads, 1) lora_shrink_stream_kernel(const StreamArgs p) {
   using SS = ShrinkStage<RM>;
   constexpr int NC = kStreamConsumers, NS = kStreamShrinkStages, TM = kStreamTM, KS = kStreamShrinkSplit;
   constexpr int KC = SS::KC, KCP = SS::KCP;
@@ -322,7 +324,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) lora_shrink_stream_kernel(c
     pdl_trigger();
     // exchange with nothing to do at all: the grid must still not complete
     // before the previous call's expand (it advances the epoch the next call reads)
-    if (p.xchg.tp > 0 && n_items == 0 && tid == 0) pdl_wait();
+    if (XCHG && n_items == 0 && tid == 0) pdl_wait();
     return;
   }
   if (tid == 0) {
@@ -385,7 +387,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) lora_shrink_stream_kernel(c
     bool ok = true;
     int f = 0;
     uint32_t epoch = 0;
-    if (p.xchg.tp > 0) {  // partials go to peers tagged with this call's epoch
+    if (XCHG) {  // partials go to peers tagged with this call's epoch
       pdl_wait();
       epoch = xchg_epoch(p.xchg);
     }
@@ -480,11 +482,13 @@ __global__ void __launch_bounds__(kStreamThreads, 1) lora_shrink_stream_kernel(c
 #pragma unroll
             for (int q = 0; q < KS; ++q) v += s_recv[par][q][r][k];
             const int row = rt.tok[t.start + r];
-            if (p.xchg.tp > 0) {  // this rank's partial value, tagged, into every rank's buffer (peer stores)
+            if (XCHG) {  // this rank's partial value, tagged, into every rank's buffer (peer stores)
               if (row < p.xchg.rows) {
                 const int64_t at = xchg_row(p.xchg, epoch, p.xchg.rank, row, p.R) + k;
                 const unsigned long long w = ((unsigned long long)(epoch + 1u) << 32) | __float_as_uint(v);
-                for (int q = 0; q < p.xchg.tp; ++q) word_store_sys(p.xchg.recv[q] + at, w);
+#pragma unroll
+                for (int q = 0; q < kMaxPeers; ++q)  // compile-time indices: no local copy of the arguments
+                  if (q < p.xchg.tp) word_store_sys(p.xchg.recv[q] + at, w);
               }
               continue;
             }
@@ -510,8 +514,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1) lora_shrink_stream_kernel(c
 // ---------------------------------------------------------------------------
 // expand
 // ---------------------------------------------------------------------------
-template <typename T, int RM>
-__global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(const __grid_constant__ StreamArgs p) {
+template <typename T, int RM, bool XCHG>
+__global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(const StreamArgs p) {
   using ES = ExpandStage<RM>;
   constexpr int NC = kStreamConsumers, NS = kStreamStages;
   constexpr int OC = ES::OC, OCP = ES::OCP, MP = ES::MP;
@@ -536,7 +540,7 @@ __global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(cons
   const int my_items = blockIdx.x < n_items ? (n_items - 1 - blockIdx.x) / G + 1 : 0;
   if (my_items == 0) {
     pdl_trigger();
-    if (p.xchg.tp > 0 && n_items == 0 && tid == 0) pdl_wait();  // as in the shrink: keep the call order
+    if (XCHG && n_items == 0 && tid == 0) pdl_wait();  // as in the shrink: keep the call order
     return;
   }
   if (tid == 0) {
@@ -548,7 +552,7 @@ __global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(cons
   }
   __syncthreads();
   pdl_trigger();
-  const bool xchg = p.xchg.tp > 0;  // mid: the sum of every rank's partials, waited for tile by tile
+  constexpr bool xchg = XCHG;  // mid: the sum of every rank's partials, polled tile by tile
 
   struct Item {
     StreamTile t;
@@ -644,7 +648,11 @@ __global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(cons
       const unsigned long long* xr = nullptr;  // exchange: this rank's buffer, row of token g (from rank 0)
       if (xchg && g < nt) {
         const int row = rt.tok[it.t.start + g];
-        xr = row < p.xchg.rows ? p.xchg.recv[p.xchg.rank] + xchg_row(p.xchg, epoch, 0, row, p.R) : nullptr;
+        unsigned long long* own = p.xchg.recv[0];
+#pragma unroll
+        for (int q = 1; q < kMaxPeers; ++q)
+          if (q == p.xchg.rank) own = p.xchg.recv[q];
+        xr = row < p.xchg.rows ? own + xchg_row(p.xchg, epoch, 0, row, p.R) : nullptr;
       }
       const int64_t xq = (int64_t)p.xchg.rows * p.R;  // words between two ranks' partial rows
       const uint32_t tag = epoch + 1u;
@@ -831,15 +839,15 @@ bool ensure_smem(K kern, int bytes, int& set, std::mutex& mu) {
   return true;
 }
 
-template <typename T, int RM>
-cudaError_t launch_stream_rm(const StreamArgs& a, cudaStream_t st, bool pdl) {
+template <typename T, int RM, bool XCHG>
+cudaError_t launch_stream_rmx(const StreamArgs& a, cudaStream_t st, bool pdl) {
   static std::mutex mu;
   static int set_s = 0, set_e = 0;
   const int route = align128(stream_routing_bytes(a.num_slots, a.S));
   const int smem_s = kStreamShrinkStages * ShrinkStage<RM>::BYTES + route;
   const int smem_e = kStreamStages * ExpandStage<RM>::BYTES + route;
-  auto ks = lora_shrink_stream_kernel<T, RM>;
-  auto ke = lora_expand_stream_kernel<T, RM>;
+  auto ks = lora_shrink_stream_kernel<T, RM, XCHG>;
+  auto ke = lora_expand_stream_kernel<T, RM, XCHG>;
   if (!ensure_smem(ks, smem_s, set_s, mu) || !ensure_smem(ke, smem_e, set_e, mu)) return cudaErrorNotSupported;
   const dim3 grid(stream_sm_count());
   if (a.phase == 2)  // expand only: mid comes from the caller (e.g. all-reduced shrink partials)
@@ -862,6 +870,11 @@ cudaError_t launch_stream_rm(const StreamArgs& a, cudaStream_t st, bool pdl) {
   if (e != cudaSuccess || a.phase == 1) return e;
   // the expand kernel always follows with the programmatic attribute: its wait is the shrink -> expand edge
   return launch_kernel(ke, grid, dim3(kStreamThreads), smem_e, st, true, a);
+}
+
+template <typename T, int RM>
+cudaError_t launch_stream_rm(const StreamArgs& a, cudaStream_t st, bool pdl) {
+  return a.xchg.tp > 0 ? launch_stream_rmx<T, RM, true>(a, st, pdl) : launch_stream_rmx<T, RM, false>(a, st, pdl);
 }
 
 }  // namespace
