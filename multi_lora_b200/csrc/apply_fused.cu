@@ -29,6 +29,17 @@
 //      and adds it, scaled, into y.
 // Each slot's A and B are read from HBM exactly once per launch. No global
 // scratch, no atomics. Every wait is bounded (status bit on timeout).
+//
+// Row-parallel instance (XCHG, tensor parallelism with the partials summed
+// over peer memory, xchg.cuh): between steps 3 and 4 the cluster's fp32
+// partial of mid (this rank's share of the input dim) goes to every rank's
+// receive buffer as tagged words, split over the cluster's CTAs by
+// destination; then every CTA polls its tile's words from all ranks in its
+// own buffer, sums them in rank order and rounds to T once. Every CTA takes a
+// ticket once it has read the epoch; the holder of the last one advances the
+// rank's epoch as it exits. A CTA
+// that waits on a peer's CTAs must not wait behind a wave of its own grid,
+// so this instance launches only when the grid fits in one wave.
 #include <cooperative_groups.h>
 
 #include <map>
@@ -40,6 +51,7 @@
 #include "kernels.h"
 #include "mma.cuh"
 #include "tma.cuh"
+#include "xchg.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -153,11 +165,93 @@ struct FlatWalk {
 // ldmatrix reads conflict-free: an odd number of 16-byte units.
 __host__ __device__ __forceinline__ int padded_row(int k) { return ((k / 8) % 2 == 0) ? k + 8 : k; }
 
+// Row-parallel gather of one tile (the XCHG instance): with the shrink on
+// (phases 0 and 1) this rank's partial -- the cluster's cs partials summed in
+// CTA order -- is published to every rank as tagged words, the destinations
+// split over the cluster's CTAs (phase 0 keeps its own value in registers
+// instead of storing it to itself); with the expand on (phases 0 and 2) mid =
+// every rank's partial summed in rank order from 0.f (the same on every rank,
+// as an all-reduce gives), rounded to T once. A partial that does not arrive
+// within the wait limit sets `s_xfail` and the timeout bit; the caller then
+// skips the expand.
+template <typename T, int RM>
+__device__ __forceinline__ void xchg_gather(const FusedArgs& p, bool shrink_on, bool expand_on, uint32_t epoch, int cs,
+                                            int j, int nt, int rank, const float* s_recv, const int* s_rows,
+                                            T (*s_mid)[RM + 8], int& s_xfail) {
+  constexpr int NT = kFusedNT, TT = kFusedTT;
+  static_assert(TT * RM <= 2 * NT, "two gather elements per thread");
+  const PeerXchg& xg = p.xchg;
+  const int tid = threadIdx.x;
+  float loc[2] = {0.f, 0.f};
+  if (shrink_on) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int e = tid + i * NT;
+      const int t = e / RM, k = e - t * RM;
+      if (e < TT * RM && t < nt && k < rank) {
+        float v = 0.f;
+        for (int q = 0; q < cs; ++q) v += s_recv[((size_t)q * TT + t) * RM + k];
+        loc[i] = v;
+        const int row = s_rows[t];
+        if (row < xg.rows) {
+          const int64_t at = xchg_row(xg, epoch, xg.rank, row, p.R) + k;
+          const unsigned long long w = tagged_word(epoch, v);
+#pragma unroll
+          for (int q = 0; q < kMaxPeers; ++q)
+            if (q < xg.tp && q % cs == j && (q != xg.rank || !expand_on)) word_store_sys(xg.recv[q] + at, w);
+        }
+      }
+    }
+  }
+  if (!expand_on) return;
+  const uint32_t tag = epoch + 1u;
+  const unsigned long long* own = xg.recv[0];
+#pragma unroll
+  for (int q = 1; q < kMaxPeers; ++q)
+    if (q == xg.rank) own = xg.recv[q];
+  const int64_t xq = (int64_t)xg.rows * p.R;  // words between two ranks' partial rows
+  const bool skip = *reinterpret_cast<volatile int*>(&s_xfail) != 0;
+  bool good = true;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int e = tid + i * NT;
+    if (e < TT * RM) {
+      const int t = e / RM, k = e - t * RM;
+      float v = 0.f;
+      if (t < nt && k < rank && !skip && s_rows[t] < xg.rows) {
+        const unsigned long long* base = own + xchg_row(xg, epoch, 0, s_rows[t], p.R) + k;
+        unsigned long long wv[kMaxPeers];
+#pragma unroll
+        for (int q = 0; q < kMaxPeers; ++q) {  // every load issued before the first poll
+          wv[q] = 0ull;
+          if (q < xg.tp && (q != xg.rank || !shrink_on)) wv[q] = word_load(base + q * xq);
+        }
+        uint64_t t0 = 0;
+#pragma unroll
+        for (int q = 0; q < kMaxPeers; ++q) {
+          if (q < xg.tp) {
+            float pq = loc[i];
+            if ((q != xg.rank || !shrink_on) && good) good = poll_word(base + q * xq, wv[q], tag, pq, t0);
+            v += pq;
+          }
+        }
+      }
+      s_mid[t][k] = Num<T>::from_f(v);
+    }
+  }
+  if (!good) {
+    s_xfail = 1;
+    flag_error(p.status, kErrTimeout);
+  }
+}
+
 // RM: rank columns covered by the tiles (16, 32 or 64; >= R). Register caps
 // (48 / 64 / 85) keep 5 / 4 / 3 CTAs per SM resident, without spills; fewer
 // registers measured faster at RM 16 (the decode shapes are latency-bound).
-template <typename T, int RM>
-__global__ void __launch_bounds__(kFusedNT, RM == 16 ? 5 : RM == 32 ? 4 : 3) apply_fused_kernel(const FusedArgs p) {
+// The exchange instance at RM 16 needs 64 (4 CTAs per SM) to stay unspilled.
+template <typename T, int RM, bool XCHG>
+__global__ void __launch_bounds__(kFusedNT, RM == 16 ? (XCHG ? 4 : 5) : RM == 32 ? 4 : 3)
+    apply_fused_kernel(const FusedArgs p) {
   constexpr int NT = kFusedNT;
   constexpr int NW = NT / 32;
   constexpr int TT = kFusedTT;    // tokens per tile (the shrink's MMA N; the expand's M rows TT..15 are zero)
@@ -203,9 +297,22 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? 5 : RM == 32 ? 4 : 3) app
   // base model (rank 0: no delta, mid untouched) or a slot this batch does not
   // use: the whole cluster leaves (uniform per cluster)
   if (rank == 0 || (sl.n == 0 && p.bs <= kFusedScan)) {
-    pdl_trigger();
+    if (XCHG && p.phase != 1) {
+      pdl_trigger();
+      if (tid == 0) {
+        pdl_wait();  // the previous call has finished counting
+        const uint32_t epoch = xchg_epoch(p.xchg);
+        xchg_advance(p.xchg, xchg_ticket(p.xchg, epoch), epoch, gridDim.x * gridDim.y * gridDim.z);
+      }
+    } else {
+      pdl_exit_early();
+    }
     return;
   }
+  // row-parallel phases: 1 publishes this rank's partial and stops, 2 skips the
+  // shrink (every rank's partial, this one's included, comes from the buffer)
+  const bool shrink_on = !XCHG || p.phase != 2;
+  const bool expand_on = !XCHG || p.phase != 1;
 
   // shared memory: A [R][kp] | B [ob_max][R] | x [TT][kp] | y [TT][ob_max] |
   //                warp partials [NW][TT][RM] f32 | partials in [cs][TT][RM] f32
@@ -231,6 +338,8 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? 5 : RM == 32 ? 4 : 3) app
     fence_barrier_init();
   }
   for (int e = tid; e < 16 * MP; e += NT) (&s_mid[0][0])[e] = Num<T>::from_f(0.f);
+  __shared__ int s_xfail;  // XCHG: a peer's partial never arrived (sticky: later tiles skip too)
+  if (XCHG && tid == 0) s_xfail = 0;
   if (klen % 16 != 0)  // half k-step at the slice end: zero the 8 pad columns of the rank rows
     for (int e = tid; e < rank * 8; e += NT) s_a[(size_t)(e / 8) * kp + klen + (e % 8)] = Num<T>::from_f(0.f);
   __syncthreads();
@@ -243,15 +352,15 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? 5 : RM == 32 ? 4 : 3) app
   // every thread -- a 1-D bulk copy costs ~80-100 ns of issue time, so one
   // thread issuing a copy per A row put ~1.5 us on the critical path.
   if (tid == 0) {
-    const uint32_t b_bytes = b_dense ? (uint32_t)olen * R * sizeof(T) : 0u;
+    const uint32_t b_bytes = b_dense && expand_on ? (uint32_t)olen * R * sizeof(T) : 0u;
     mbar_arrive_expect_tx(&bar_w, b_bytes);
     if (b_bytes > 0) bulk_copy_g2s(s_b, b_src, b_bytes, &bar_w);
   }
-  if (klen > 0)
+  if (klen > 0 && shrink_on)
     for (FlatWalk w(tid, NT, klen / 8); w.r < rank; w.next())
       cp_async16(s_a + (size_t)w.r * kp + w.c * 8, a_src + (int64_t)w.r * p.in_dim + w.c * 8);
   const int rc = (rank + 7) / 8;  // 16-byte B chunks per row that hold rank columns
-  if (!b_dense) {  // rows of R with only `rank` valid columns: 16-byte copies per thread
+  if (!b_dense && expand_on) {  // rows of R with only `rank` valid columns: 16-byte copies per thread
     for (int e = tid; e < olen * rc; e += NT) {
       const int row = e / rc, c = e - row * rc;
       cp_async16(s_b + (size_t)row * R + c * 8, b_src + (int64_t)row * R + c * 8);
@@ -260,6 +369,10 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? 5 : RM == 32 ? 4 : 3) app
   cp_async_commit();  // group: this CTA's weights
   pdl_trigger();
   pdl_wait();  // x and y come from earlier kernels
+  const uint32_t epoch = XCHG ? xchg_epoch(p.xchg) : 0u;  // after the wait: the previous call has advanced it
+  const bool counts = XCHG && p.phase != 1 && tid == 0;     // this CTA's ticket in the call's count
+  uint32_t ticket = 0u;
+  bool ticketed = false;
 
   const T* __restrict__ xbase = static_cast<const T*>(p.x);
   T* __restrict__ ybase = static_cast<T*>(m.y);
@@ -284,14 +397,14 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? 5 : RM == 32 ? 4 : 3) app
       if (klen % 16 != 0)  // pad columns: disjoint from the x rows loaded below
         for (int e = tid; e < TT * 8; e += NT) s_x[(size_t)(e / 8) * kp + klen + (e % 8)] = Num<T>::from_f(0.f);
       if (!scanned_rows) __syncthreads();
-      if (m.y_tma && olen > 0) {  // this tile's y rows (output block), needed only by the expand
+      if (m.y_tma && olen > 0 && expand_on) {  // this tile's y rows (output block), needed only by the expand
         for (FlatWalk w(tid, NT, olen / 8); w.r < nt; w.next())
           cp_async16(s_y + (size_t)w.r * p.ob_max + w.c * 8,
                      ybase + (int64_t)s_rows[w.r] * m.y_stride + o_lo + w.c * 8);
       }
       cp_async_commit();  // group: this tile's y rows (possibly empty)
       {  // this tile's x rows (k-slice): plain 16-byte loads by every thread (L2 hits)
-        if (klen > 0)
+        if (klen > 0 && shrink_on)
           for (FlatWalk w(tid, NT, klen / 8); w.r < nt; w.next()) {
             const uint4 v =
                 __ldcg(reinterpret_cast<const uint4*>(xbase + (int64_t)s_rows[w.r] * p.x_stride + k0) + w.c);
@@ -338,7 +451,7 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? 5 : RM == 32 ? 4 : 3) app
             }
           }
         };
-        if (ok) {
+        if (ok && shrink_on) {
           // two accumulator chains (alternate steps) halve the dependent MMA chain
           for (int kk = warp; kk < ksteps; kk += 2 * NW) {
             kstep(kk * 16, acc0);
@@ -362,37 +475,47 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? 5 : RM == 32 ? 4 : 3) app
       __syncthreads();  // warp partials complete
       if (first) cluster_wait_acquire();  // every peer runs and has its barriers initialised
       first = false;
+      if (counts && !ticketed) {  // the epoch load has long returned
+        ticket = xchg_ticket(p.xchg, epoch);
+        ticketed = true;
+      }
       // ---- push this CTA's partial (its warps' partials summed in warp order) into
       //      slot j of every peer's receive buffer ----
-      if (tid == 0) mbar_arrive_expect_tx(&bar_p, (uint32_t)cs * nt * RM * sizeof(float));
-      if (tid < nt * Q4) {
-        const int t = tid / Q4, k4 = (tid - t * Q4) * 4;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (shrink_on) {  // phase 2 has no shrink
+        if (tid == 0) mbar_arrive_expect_tx(&bar_p, (uint32_t)cs * nt * RM * sizeof(float));
+        if (tid < nt * Q4) {
+          const int t = tid / Q4, k4 = (tid - t * Q4) * 4;
+          float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-        for (int w = 0; w < NW; ++w) {
-          const float4 u = *reinterpret_cast<const float4*>(s_wred + ((size_t)w * TT + t) * RM + k4);
-          v.x += u.x;
-          v.y += u.y;
-          v.z += u.z;
-          v.w += u.w;
+          for (int w = 0; w < NW; ++w) {
+            const float4 u = *reinterpret_cast<const float4*>(s_wred + ((size_t)w * TT + t) * RM + k4);
+            v.x += u.x;
+            v.y += u.y;
+            v.z += u.z;
+            v.w += u.w;
+          }
+          const uint32_t dst = smem_addr(s_recv + ((size_t)j * TT + t) * RM + k4);
+          const uint32_t bar = smem_addr(&bar_p);
+          for (int q = 0; q < cs; ++q)
+            st_async_v4(cluster_map(dst, (uint32_t)q), v.x, v.y, v.z, v.w, cluster_map(bar, (uint32_t)q));
         }
-        const uint32_t dst = smem_addr(s_recv + ((size_t)j * TT + t) * RM + k4);
-        const uint32_t bar = smem_addr(&bar_p);
-        for (int q = 0; q < cs; ++q)
-          st_async_v4(cluster_map(dst, (uint32_t)q), v.x, v.y, v.z, v.w, cluster_map(bar, (uint32_t)q));
+        ok = mbar_wait(&bar_p, p_phase, p.status) && ok;
+        p_phase ^= 1u;
       }
-      ok = mbar_wait(&bar_p, p_phase, p.status) && ok;
-      p_phase ^= 1u;
-      // ---- gather: mid = sum of the cs partials in CTA order, rounded to T once ----
-      for (int e = tid; e < TT * RM; e += NT) {
-        const int t = e / RM, k = e - t * RM;
-        float v = 0.f;
-        if (t < nt && k < rank) {
-          for (int q = 0; q < cs; ++q) v += s_recv[((size_t)q * TT + t) * RM + k];
-          if (j == 0 && m.mid != nullptr)
-            static_cast<T*>(m.mid)[(int64_t)s_rows[t] * m.mid_stride + k] = Num<T>::from_f(v);
+      if constexpr (XCHG) {
+        xchg_gather<T, RM>(p, shrink_on, expand_on, epoch, cs, j, nt, rank, s_recv, s_rows, s_mid, s_xfail);
+      } else {
+        // ---- gather: mid = sum of the cs partials in CTA order, rounded to T once ----
+        for (int e = tid; e < TT * RM; e += NT) {
+          const int t = e / RM, k = e - t * RM;
+          float v = 0.f;
+          if (t < nt && k < rank) {
+            for (int q = 0; q < cs; ++q) v += s_recv[((size_t)q * TT + t) * RM + k];
+            if (j == 0 && m.mid != nullptr)
+              static_cast<T*>(m.mid)[(int64_t)s_rows[t] * m.mid_stride + k] = Num<T>::from_f(v);
+          }
+          s_mid[t][k] = Num<T>::from_f(v);
         }
-        s_mid[t][k] = Num<T>::from_f(v);
       }
       if (b_pending) {  // the dense B block, needed from here on, landed during the shrink
         ok = mbar_wait(&bar_w, 0, p.status) && ok;
@@ -401,7 +524,7 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? 5 : RM == 32 ? 4 : 3) app
       if (m.y_tma && olen > 0) cp_async_wait<0>();  // y rows staged during the shrink and exchange
       __syncthreads();  // s_mid, B and the staged y rows complete
       // ---- expand: this CTA's output block on tensor cores, fused scaling + residual ----
-      if (ok) {
+      if (ok && expand_on && (!XCHG || s_xfail == 0)) {
         uint32_t am[RM / 16][4];
 #pragma unroll
         for (int kk = 0; kk < RM / 16; ++kk)
@@ -506,11 +629,15 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? 5 : RM == 32 ? 4 : 3) app
   if (b_pending) mbar_wait(&bar_w, 0, p.status);
   cp_async_wait<0>();
   if (!ok && tid == 0) mbar_wait(&bar_p, p_phase ^ 1u, p.status);  // ok is only cleared inside a tile
+  if (counts) {
+    if (!ticketed) ticket = xchg_ticket(p.xchg, epoch);  // no tile of this slot in any scan pass
+    xchg_advance(p.xchg, ticket, epoch, gridDim.x * gridDim.y * gridDim.z);
+  }
 }
 
 namespace {
 
-template <typename T, int RM>
+template <typename T, int RM, bool XCHG>
 struct FusedLauncher {
   std::mutex mu;
   int smem_set = 0;
@@ -520,7 +647,7 @@ struct FusedLauncher {
   // Resident CTAs per SM for this shape (0 when a cluster of cs cannot be placed).
   int occupancy(int cs, size_t smem) {
     std::lock_guard<std::mutex> lock(mu);
-    auto kern = apply_fused_kernel<T, RM>;
+    auto kern = apply_fused_kernel<T, RM, XCHG>;
     const int kib = (int)((smem + 1023) / 1024);
     auto key = std::make_pair(cs, kib);
     auto it = occ.find(key);
@@ -567,7 +694,7 @@ struct FusedLauncher {
   }
 
   cudaError_t launch(const FusedArgs& a, int cs, size_t smem, cudaStream_t st, bool pdl) {
-    auto kern = apply_fused_kernel<T, RM>;
+    auto kern = apply_fused_kernel<T, RM, XCHG>;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(cs, a.num_slots, a.n_mod);
     cfg.blockDim = dim3(kFusedNT);
@@ -586,9 +713,9 @@ struct FusedLauncher {
   }
 };
 
-template <typename T, int RM>
-FusedLauncher<T, RM>& launcher() {
-  static FusedLauncher<T, RM> l;
+template <typename T, int RM, bool XCHG>
+FusedLauncher<T, RM, XCHG>& launcher() {
+  static FusedLauncher<T, RM, XCHG> l;
   return l;
 }
 
@@ -610,9 +737,9 @@ int sm_count() {
   return n;
 }
 
-template <typename T, int RM>
-cudaError_t launch_rm(FusedArgs a, cudaStream_t st, bool pdl) {
-  auto& l = launcher<T, RM>();
+template <typename T, int RM, bool XCHG>
+cudaError_t launch_rmx(FusedArgs a, cudaStream_t st, bool pdl) {
+  auto& l = launcher<T, RM, XCHG>();
   // Cluster size: fewest waves of CTAs for the whole launch (every slot counted,
   // since which slots the batch uses is only known on the device); ties go to
   // the size closest to 8 (8, 16, 4, 2): on B200, clusters of 16 at the same
@@ -642,6 +769,7 @@ cudaError_t launch_rm(FusedArgs a, cudaStream_t st, bool pdl) {
     if (per_sm <= 0) continue;
     const long long ctas = (long long)c.n_mod * c.num_slots * cs;
     const int waves = (int)((ctas + (long long)sm_count() * per_sm - 1) / ((long long)sm_count() * per_sm));
+    if (XCHG && waves > 1) continue;  // its CTAs wait on peers' CTAs: the whole grid must be resident
     auto pref = [](int c) { return c == 8 ? 0 : c == 16 ? 1 : c == 4 ? 2 : 3; };
     if (waves < best_waves || (waves == best_waves && pref(cs) < pref(best_cs))) {
       c.ks = ks;
@@ -656,6 +784,11 @@ cudaError_t launch_rm(FusedArgs a, cudaStream_t st, bool pdl) {
   return l.launch(best, best_cs, best_smem, st, pdl);
 }
 
+template <typename T, int RM>
+cudaError_t launch_rm(const FusedArgs& a, cudaStream_t st, bool pdl) {
+  return a.xchg.tp > 0 ? launch_rmx<T, RM, true>(a, st, pdl) : launch_rmx<T, RM, false>(a, st, pdl);
+}
+
 }  // namespace
 
 // Returns cudaErrorNotSupported when the shape is outside the fused kernel's
@@ -664,6 +797,7 @@ cudaError_t launch_apply_fused(FusedArgs a, int dtype, cudaStream_t st, bool pdl
   if (dtype != kBF16 && dtype != kF16) return cudaErrorNotSupported;
   if (a.n_mod < 1 || a.n_mod > kMaxFusedModules) return cudaErrorNotSupported;
   if (a.R > 64 || a.R % 8 != 0 || a.in_dim % 8 != 0) return cudaErrorNotSupported;
+  if (a.xchg.tp > 0 && (a.n_mod != 1 || a.phase < 0 || a.phase > 2)) return cudaErrorNotSupported;
   const int rm = a.R <= 16 ? 16 : a.R <= 32 ? 32 : 64;
   if (dtype == kBF16)
     return rm == 16 ? launch_rm<__nv_bfloat16, 16>(a, st, pdl)

@@ -39,6 +39,7 @@
 #include "kernels.h"
 #include "mma.cuh"
 #include "tma.cuh"
+#include "xchg.cuh"
 
 namespace mlora {
 
@@ -243,58 +244,6 @@ __device__ __forceinline__ StreamModule stream_module(const StreamArgs& p, int m
   return r;
 }
 
-// ---- peer exchange (row-parallel tensor parallelism) ----
-// Every partial value goes to every rank as one 8-byte word {fp32 bits, tag}
-// with tag = epoch + 1 of the call; the reader polls its words until the tag
-// is this call's. The epoch is the number of calls the expand kernel has
-// completed; the words alternate between two halves by epoch parity, so a
-// rank one call ahead never overwrites words still being read.
-__device__ __forceinline__ void word_store_sys(unsigned long long* w, unsigned long long v) {
-  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(w), "l"(v) : "memory");
-}
-__device__ __forceinline__ void word_load_pair(const unsigned long long* w, unsigned long long& a,
-                                               unsigned long long& b) {
-  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(w) : "memory");
-}
-// The call's epoch: read after griddepcontrol.wait, when every earlier call's
-// expand kernel (which advances the counter) has completed.
-__device__ __forceinline__ uint32_t xchg_epoch(const PeerXchg& x) {
-  return *reinterpret_cast<volatile const uint32_t*>(x.ctr);
-}
-// Offset (words) of partial row `row` from rank `from` in a receive buffer.
-__device__ __forceinline__ int64_t xchg_row(const PeerXchg& x, uint32_t epoch, int from, int row, int R) {
-  return ((int64_t)(epoch & 1u) * x.tp * x.rows + (int64_t)from * x.rows + row) * R;
-}
-// Two adjacent words (columns c, c + 1 of one rank's row), polled until both
-// carry `tag` (each column only if it is below `live`); bounded by
-// kWaitLimitNs from `t0`. Returns false on timeout.
-__device__ __forceinline__ bool poll_pair(const unsigned long long* w, uint32_t tag, int c, int live, float& v0,
-                                          float& v1, uint64_t& t0) {
-  unsigned long long a, b;
-  word_load_pair(w, a, b);
-  const bool need0 = c < live, need1 = c + 1 < live;
-  while ((need0 && (uint32_t)(a >> 32) != tag) || (need1 && (uint32_t)(b >> 32) != tag)) {
-    if (t0 == 0) t0 = global_timer_ns();
-    else if (global_timer_ns() - t0 > kWaitLimitNs) return false;
-    word_load_pair(w, a, b);
-  }
-  v0 = need0 ? __uint_as_float((uint32_t)a) : 0.f;
-  v1 = need1 ? __uint_as_float((uint32_t)b) : 0.f;
-  return true;
-}
-// Counts the expand kernel's CTAs that had items (`working` of them); the
-// last one advances the epoch. Only CTAs with items count: each of them read
-// the epoch after its griddepcontrol.wait, and that wait already implies the
-// previous call's expand kernel completed, so two calls never count at once.
-__device__ __forceinline__ void xchg_cta_done(const PeerXchg& x, uint32_t working) {
-  __threadfence();
-  if (atomicAdd(&x.ctr[1], 1u) == working - 1u) {
-    x.ctr[1] = 0u;
-    x.ctr[0] = x.ctr[0] + 1u;
-    __threadfence();
-  }
-}
-
 // ---------------------------------------------------------------------------
 // shrink
 // ---------------------------------------------------------------------------
@@ -321,10 +270,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1) lora_shrink_stream_kernel(c
   const int crank = (int)(blockIdx.x % KS), cl = (int)(blockIdx.x / KS), NCL = (int)(gridDim.x / KS);
   const int my_items = cl < n_items ? (n_items - 1 - cl) / NCL + 1 : 0;  // the same for the whole cluster
   if (my_items == 0) {
-    pdl_trigger();
-    // exchange with nothing to do at all: the grid must still not complete
-    // before the previous call's expand (it advances the epoch the next call reads)
-    if (XCHG && n_items == 0 && tid == 0) pdl_wait();
+    // CTA 0 waits even here: the grid must not complete before the previous
+    // kernel (with the exchange on, the previous call's expand advances the
+    // epoch the next call reads)
+    pdl_exit_early();
     return;
   }
   if (tid == 0) {
@@ -539,8 +488,7 @@ __global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(cons
   const int G = gridDim.x;
   const int my_items = blockIdx.x < n_items ? (n_items - 1 - blockIdx.x) / G + 1 : 0;
   if (my_items == 0) {
-    pdl_trigger();
-    if (XCHG && n_items == 0 && tid == 0) pdl_wait();  // as in the shrink: keep the call order
+    pdl_exit_early();  // as in the shrink: keep the call order
     return;
   }
   if (tid == 0) {

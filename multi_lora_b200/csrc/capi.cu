@@ -76,6 +76,8 @@ int check_meta(const mlora_kernel_input_metadata_t* m, int64_t rows) {
 
 namespace mlora {
 int report_error(int code, const char* msg) { return fail(code, "%s", msg); }
+int forced_apply_path() { return apply_path_override(); }
+void note_apply_path(int path) { g_last_apply_path = path; }
 }  // namespace mlora
 
 extern "C" {

@@ -41,6 +41,15 @@ __device__ __forceinline__ void pdl_wait() {
 __device__ __forceinline__ void pdl_trigger() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
+// Early exit of a CTA that touches nothing earlier kernels write. CTA 0 of
+// the grid still waits for the previous kernel (every CTA that works waits on
+// its own path), so a grid never completes before its predecessor: a kernel
+// that waits for this one also waits for every kernel before it, even when no
+// CTA of this grid had work.
+__device__ __forceinline__ void pdl_exit_early() {
+  pdl_trigger();
+  if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x == 0) pdl_wait();
+}
 
 template <typename T>
 struct Num;

@@ -67,6 +67,17 @@ struct RmsNormArgs {
   int64_t res_stride;
 };
 
+// Tensor-parallel exchange of row-parallel shrink partials over peer memory
+// (buffers of mlora_peer_exchange_t, include/mlora_b200.h). tp == 0: off.
+// A partial value travels in one 8-byte word: the fp32 bits in the low half,
+// the call's tag (epoch + 1) in the high half, written and read as one
+// single-copy-atomic 8-byte access, so the reader needs no separate flag.
+constexpr int kMaxPeers = 8;
+struct PeerXchg {
+  unsigned long long* recv[kMaxPeers];  // rank q's words [2][tp][rows][R], mapped in this process
+  uint32_t* ctr;                        // this rank's counters: [0] epoch (calls completed), [1] CTAs of the call's last kernel that finished
+  int tp, rank, rows;
+};
 // One projection of a fused apply_lora launch; up to kMaxFusedModules
 // projections that share x and the routing go in one launch (e.g. q/k/v).
 constexpr int kMaxFusedModules = 4;
@@ -96,6 +107,11 @@ struct FusedArgs {
   int ks;                 // input columns per cluster CTA (multiple of 8), set by the launcher
   int ob_max;             // largest module ob (sizes the shared-memory B and y tiles)
   uint32_t* status;
+  // tp > 0 (one projection): row-parallel exchange. The cluster's partial of
+  // mid goes to every rank's buffer and mid is the sum of all ranks' partials.
+  // phase 0: both in one launch; 1: publish only; 2: wait and expand only.
+  PeerXchg xchg;
+  int phase;
 };
 
 cudaError_t launch_apply_fused(FusedArgs a, int dtype, cudaStream_t st, bool pdl);
@@ -103,17 +119,6 @@ cudaError_t launch_apply_fused(FusedArgs a, int dtype, cudaStream_t st, bool pdl
 // Streaming apply (persistent shrink + expand kernels, csrc/apply_stream.cu).
 constexpr int kMaxStreamModules = 4;
 
-// Tensor-parallel exchange of row-parallel shrink partials over peer memory
-// (buffers of mlora_peer_exchange_t, include/mlora_b200.h). tp == 0: off.
-// A partial value travels in one 8-byte word: the fp32 bits in the low half,
-// the call's tag (epoch + 1) in the high half, written and read as one
-// single-copy-atomic 8-byte access, so the reader needs no separate flag.
-constexpr int kMaxPeers = 8;
-struct PeerXchg {
-  unsigned long long* recv[kMaxPeers];  // rank q's words [2][tp][rows][R], mapped in this process
-  uint32_t* ctr;                        // this rank's counters: [0] epoch (calls completed), [1] finished expand CTAs
-  int tp, rank, rows;
-};
 struct StreamModule {
   const void* a;          // A stack [K, R, in], contiguous
   const void* b;          // B stack [K, out, R], contiguous
@@ -190,6 +195,10 @@ cudaError_t launch_apply_prefill(const PrefillLaunch& l, int dtype, cudaStream_t
 
 // Sets the message mlora_last_error() returns on this thread; returns `code`.
 int report_error(int code, const char* msg);
+// The apply path forced by mlora_set_apply_path / MLORA_APPLY_PATH (0:
+// automatic), and the one this thread's last call ran (mlora_last_apply_path).
+int forced_apply_path();
+void note_apply_path(int path);
 cudaError_t launch_shrink(const ShrinkArgs& a, int dtype, bool out_f32, cudaStream_t st, bool pdl);
 cudaError_t launch_expand(const ExpandArgs& a, int dtype, bool mid_f32, cudaStream_t st, bool pdl);
 cudaError_t launch_rmsnorm(const RmsNormArgs& a, int dtype, cudaStream_t st, bool pdl);

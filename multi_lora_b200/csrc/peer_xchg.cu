@@ -1,7 +1,8 @@
 // Row-parallel projections with the shrink partials exchanged over peer
 // memory (include/mlora_b200.h: mlora_peer_exchange_t and friends): buffer
-// set-up through CUDA IPC, and the entry point that launches the streaming
-// shrink/expand pair in exchange mode (csrc/apply_stream.cu).
+// set-up through CUDA IPC, and the entry point that launches the fused decode
+// kernel (csrc/apply_fused.cu) or the streaming shrink/expand pair
+// (csrc/apply_stream.cu) in exchange mode.
 #include <cstring>
 
 #include "../../include/mlora_b200.h"
@@ -91,6 +92,54 @@ int mlora_row_parallel_apply_p2p(const void* x, int64_t rows, int64_t in_shard, 
   if (meta->bs == 0 || rows == 0) return MLORA_OK;
 
   const XLayout L(X.tp, X.max_rows, X.max_rank);
+  mlora::PeerXchg xc{};
+  xc.tp = X.tp;
+  xc.rank = X.rank;
+  xc.rows = X.max_rows;
+  for (int q = 0; q < X.tp; ++q)
+    xc.recv[q] = reinterpret_cast<unsigned long long*>(static_cast<unsigned char*>(X.buffers[q]) + L.recv);
+  xc.ctr = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(X.buffers[X.rank]) + L.ctr);
+  const bool pdl = mlora_get_pdl() != 0;
+
+  // Decode batches: the fused kernel (one launch: shrink, exchange, expand),
+  // as mlora_apply_lora picks it; it declines shapes whose grid does not fit
+  // in one wave. Otherwise the streaming pair.
+  const int forced = mlora::forced_apply_path();
+  const bool fused_pref = forced == 1 || (forced == 0 && rows < 256 && meta->max_len <= 16 &&
+                                          rows <= 64LL * meta->num_slots);
+  if (fused_pref) {
+    mlora::FusedArgs f{};
+    f.x = x;
+    f.x_stride = x_row_stride;
+    f.n_mod = 1;
+    f.mod[0].a = a_shard;
+    f.mod[0].b = b_shard;
+    f.mod[0].y = y;
+    f.mod[0].y_stride = y_row_stride;
+    f.mod[0].mid = nullptr;
+    f.mod[0].mid_stride = max_rank;
+    f.mod[0].out_dim = (int)out_cols;
+    f.seg_indptr = meta->seg_indptr;
+    f.weight_indices = meta->weight_indices;
+    f.lora_ranks = meta->lora_ranks;
+    f.scalings = meta->scalings;
+    f.scalings_dtype = meta->scalings_dtype;
+    f.bs = meta->bs;
+    f.S = (int)rows;
+    f.in_dim = (int)in_shard;
+    f.R = (int)max_rank;
+    f.num_slots = meta->num_slots;
+    f.status = status;
+    f.xchg = xc;
+    f.phase = phase;
+    const cudaError_t e = mlora::launch_apply_fused(f, dtype, (cudaStream_t)stream, pdl);
+    if (e == cudaSuccess) {
+      mlora::note_apply_path(1);
+      return MLORA_OK;
+    }
+    if (e != cudaErrorNotSupported) return cuda_rc(e);
+  }
+
   mlora::StreamArgs sa{};
   sa.x = x;
   sa.x_stride = x_row_stride;
@@ -115,14 +164,10 @@ int mlora_row_parallel_apply_p2p(const void* x, int64_t rows, int64_t in_shard, 
   sa.R = (int)max_rank;
   sa.num_slots = meta->num_slots;
   sa.status = status;
-  sa.xchg.tp = X.tp;
-  sa.xchg.rank = X.rank;
-  sa.xchg.rows = X.max_rows;
-  for (int q = 0; q < X.tp; ++q)
-    sa.xchg.recv[q] = reinterpret_cast<unsigned long long*>(static_cast<unsigned char*>(X.buffers[q]) + L.recv);
-  sa.xchg.ctr = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(X.buffers[X.rank]) + L.ctr);
-  const cudaError_t e = mlora::launch_apply_stream(sa, dtype, (cudaStream_t)stream, mlora_get_pdl() != 0);
+  sa.xchg = xc;
+  const cudaError_t e = mlora::launch_apply_stream(sa, dtype, (cudaStream_t)stream, pdl);
   if (e == cudaErrorNotSupported) return xfail(MLORA_ERR_INVALID_ARGUMENT, "shape outside the exchange path");
+  if (e == cudaSuccess) mlora::note_apply_path(3);
   return cuda_rc(e);
 }
 

@@ -126,7 +126,7 @@ __global__ void __launch_bounds__(kTcThreads) lora_shrink_tc_kernel(const __grid
   }
   __syncthreads();
   if (!s_ok) {  // uniform over the cluster (same tile)
-    pdl_trigger();
+    pdl_exit_early();
     return;
   }
   const TcTile t = s_tile;
@@ -318,7 +318,7 @@ __global__ void __launch_bounds__(kTcThreads) lora_expand_tc_kernel(const __grid
   }
   __syncthreads();
   if (!s_ok) {
-    pdl_trigger();
+    pdl_exit_early();
     return;
   }
   const TcTile t = s_tile;

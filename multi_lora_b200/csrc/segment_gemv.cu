@@ -49,7 +49,7 @@ __global__ void __launch_bounds__(NT) shrink_kernel(const ShrinkArgs p) {
   }
   const int rows_eff = min(p.max_rank, rank * p.stack_num);
   if (row0 >= rows_eff) {
-    pdl_trigger();
+    pdl_exit_early();
     return;
   }
   const int nrows = min(RPC, rows_eff - row0);
@@ -174,7 +174,7 @@ __global__ void __launch_bounds__(NT) expand_kernel(const ExpandArgs p) {
     rank = rank < 0 ? 0 : p.max_rank;
   }
   if (rank == 0) {
-    pdl_trigger();
+    pdl_exit_early();
     return;
   }
   float scale;

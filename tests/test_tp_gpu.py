@@ -9,7 +9,9 @@
 * the peer-memory exchange with 2 and 4 ranks emulated on one GPU (every
   rank's shrink-and-publish phase, then every rank's wait-and-expand phase, so
   no kernel waits for one queued after it), repeated calls, inside a CUDA
-  graph, and the bounded wait running out on partials that no rank writes.
+  graph, one rank's single-launch call between the others' two phases, and
+  the bounded wait running out on partials that no rank writes; each on the
+  fused decode kernel and on the streaming pair.
 
 Tolerance: bf16 within atol 2e-2 / rtol 1e-2 of the fp32-accumulated
 reference (the parity bar for bf16 outputs).
@@ -26,6 +28,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
+from multi_lora_b200 import _native
 from multi_lora_b200.backend import CudaLoRABackend
 from multi_lora_b200.batch_info import KernelInputMetaData
 from multi_lora_b200.tensor_parallel import (COLUMN, ROW, PeerExchange, row_parallel_apply, row_parallel_apply_p2p,
@@ -35,6 +38,21 @@ from oracle import lora_oracle as orc
 pytestmark = pytest.mark.gpu
 
 TOL = dict(atol=2e-2, rtol=1e-2)
+PATHS = {"fused": 1, "stream": 3}  # mlora_last_apply_path codes of the exchange's two kernels
+
+
+class forced_path:
+    """Force the apply path tried first (mlora_set_apply_path) inside a with-block."""
+
+    def __init__(self, name):
+        self.name = name
+
+    def __enter__(self):
+        self.old = _native.get_apply_path()
+        _native.set_apply_path(self.name)
+
+    def __exit__(self, *exc):
+        _native.set_apply_path(self.old)
 
 
 def _case(seed=0, S=64, IN=1024, OUT=768, K=8, R=16):
@@ -128,15 +146,18 @@ def _p2p_setup(dev, tp, c):
     return bes, ranks
 
 
-def _p2p_call(bes, ranks, xs, y_parts):
+def _p2p_call(bes, ranks, xs, y_parts, path=None):
     """All ranks' shrink-and-publish phase, then all ranks' wait-and-expand phase."""
     for phase in (1, 2):
         for p, (xp, a_s, b_s, lo, hi) in enumerate(ranks):
             row_parallel_apply_p2p(bes[p], xp, a_s, b_s, y_parts[p][:, lo:hi], xs[p], phase=phase)
+            if path is not None:
+                assert _native.capi().mlora_last_apply_path() == PATHS[path]
 
 
+@pytest.mark.parametrize("path", sorted(PATHS))
 @pytest.mark.parametrize("tp", [2, 4])
-def test_p2p_exchange_emulated_one_gpu(cuda_dev, tp):
+def test_p2p_exchange_emulated_one_gpu(cuda_dev, tp, path):
     """Sum over ranks of the pre-all-reduce outputs = the unsharded delta; three
     calls in a row (epochs 1..3, both halves of the double-buffered partials)."""
     dev = cuda_dev
@@ -147,7 +168,8 @@ def test_p2p_exchange_emulated_one_gpu(cuda_dev, tp):
     try:
         for _ in range(3):
             y_parts = [torch.zeros(c["y"].shape, dtype=torch.bfloat16, device=dev) for _ in range(tp)]
-            _p2p_call(bes, ranks, xs, y_parts)
+            with forced_path(path):
+                _p2p_call(bes, ranks, xs, y_parts, path)
             torch.cuda.synchronize()
             for p, (_, _, _, lo, hi) in enumerate(ranks):  # each rank wrote only its columns
                 assert (y_parts[p][:, :lo] == 0).all() and (y_parts[p][:, hi:] == 0).all()
@@ -159,7 +181,8 @@ def test_p2p_exchange_emulated_one_gpu(cuda_dev, tp):
         xs[0].close()
 
 
-def test_p2p_exchange_in_cuda_graph(cuda_dev):
+@pytest.mark.parametrize("path", sorted(PATHS))
+def test_p2p_exchange_in_cuda_graph(cuda_dev, path):
     """The exchange captured once and replayed: the epoch advances on the device."""
     dev = cuda_dev
     c = _case(seed=6)
@@ -169,13 +192,14 @@ def test_p2p_exchange_in_cuda_graph(cuda_dev):
     ref = torch.from_numpy(_ref_delta(c))
     y_parts = [torch.zeros(c["y"].shape, dtype=torch.bfloat16, device=dev) for _ in range(tp)]
     try:
-        _p2p_call(bes, ranks, xs, y_parts)  # eager once (epoch 1)
-        torch.cuda.synchronize()
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            for y in y_parts:
-                y.zero_()
-            _p2p_call(bes, ranks, xs, y_parts)
+        with forced_path(path):
+            _p2p_call(bes, ranks, xs, y_parts, path)  # eager once (epoch 1)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for y in y_parts:
+                    y.zero_()
+                _p2p_call(bes, ranks, xs, y_parts)
         for _ in range(3):
             g.replay()
             torch.cuda.synchronize()
@@ -188,7 +212,37 @@ def test_p2p_exchange_in_cuda_graph(cuda_dev):
         xs[0].close()
 
 
-def test_p2p_exchange_wait_times_out_and_reports(cuda_dev):
+@pytest.mark.parametrize("path", sorted(PATHS))
+@pytest.mark.parametrize("tp", [2, 4])
+def test_p2p_single_launch_between_phases(cuda_dev, tp, path):
+    """Rank 0 runs the whole call in one go (phase 0: publish, wait, expand)
+    after every other rank published and before they expand, so its waits
+    find every partial already there; two calls in a row."""
+    dev = cuda_dev
+    c = _case(seed=8)
+    bes, ranks = _p2p_setup(dev, tp, c)
+    xs = PeerExchange.local_group(tp, device=dev, max_rows=64, max_rank=16)
+    ref = torch.from_numpy(_ref_delta(c))
+    try:
+        for _ in range(2):
+            y_parts = [torch.zeros(c["y"].shape, dtype=torch.bfloat16, device=dev) for _ in range(tp)]
+            with forced_path(path):
+                for phase, who in ((1, range(1, tp)), (0, [0]), (2, range(1, tp))):
+                    for p in who:
+                        xp, a_s, b_s, lo, hi = ranks[p]
+                        row_parallel_apply_p2p(bes[p], xp, a_s, b_s, y_parts[p][:, lo:hi], xs[p], phase=phase)
+                        assert _native.capi().mlora_last_apply_path() == PATHS[path]
+            torch.cuda.synchronize()
+            delta = torch.stack([y.float() for y in y_parts]).sum(0).cpu()
+            torch.testing.assert_close(delta, ref, **TOL)
+        for be in bes:
+            be.check_routing()
+    finally:
+        xs[0].close()
+
+
+@pytest.mark.parametrize("path", sorted(PATHS))
+def test_p2p_exchange_wait_times_out_and_reports(cuda_dev, path):
     """A rank whose peer never publishes: its bounded polls run out (about 2 s),
     the status word carries the timeout bit, the tile is skipped, the context
     stays usable."""
@@ -199,8 +253,10 @@ def test_p2p_exchange_wait_times_out_and_reports(cuda_dev):
     try:
         y = torch.zeros(c["y"].shape, dtype=torch.bfloat16, device=dev)
         xp, a_s, b_s, lo, hi = ranks[0]
-        row_parallel_apply_p2p(bes[0], xp, a_s, b_s, y[:, lo:hi], xs[0], phase=1)
-        row_parallel_apply_p2p(bes[0], xp, a_s, b_s, y[:, lo:hi], xs[0], phase=2)  # rank 1 never published
+        with forced_path(path):
+            row_parallel_apply_p2p(bes[0], xp, a_s, b_s, y[:, lo:hi], xs[0], phase=1)
+            row_parallel_apply_p2p(bes[0], xp, a_s, b_s, y[:, lo:hi], xs[0], phase=2)  # rank 1 never published
+            assert _native.capi().mlora_last_apply_path() == PATHS[path]
         torch.cuda.synchronize()
         assert int(bes[0].status_word(dev).item()) & 0x10
         assert (y == 0).all()  # nothing expanded from a missing partial
@@ -234,7 +290,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _nccl_worker(rank, world, port, q, exchange=False):
+def _nccl_worker(rank, world, port, q, exchange=None):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     torch.cuda.set_device(rank)
@@ -249,6 +305,8 @@ def _nccl_worker(rank, world, port, q, exchange=False):
         ilo, ihi = shard_bounds(x.shape[1], rank, world)
         y_part = torch.zeros(c["y"].shape, dtype=torch.bfloat16, device=dev)
         xchg = PeerExchange.create(device=dev, max_rows=64, max_rank=16) if exchange else None
+        if exchange:
+            _native.set_apply_path(exchange)
         for _ in range(3):  # repeated: the resident partial buffer (or the exchange's halves) is reused
             y_part.zero_()
             row_parallel_apply(be, x[:, ilo:ihi].contiguous(), a_s, b_s, y_part, rank, world, exchange=xchg)
@@ -267,7 +325,8 @@ def _nccl_worker(rank, world, port, q, exchange=False):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("exchange", [False, True], ids=["nccl_allreduce", "peer_exchange"])
+@pytest.mark.parametrize("exchange", [None, "fused", "stream"],
+                         ids=["nccl_allreduce", "peer_exchange_fused", "peer_exchange_stream"])
 def test_tp_nccl_row_parallel(exchange):
     world = 2
     ctx = mp.get_context("spawn")
