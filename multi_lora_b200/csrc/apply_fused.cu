@@ -35,9 +35,10 @@
 // partial of mid (this rank's share of the input dim) goes to every rank's
 // receive buffer as tagged words, split over the cluster's CTAs by
 // destination; then every CTA polls its tile's words from all ranks in its
-// own buffer, sums them in rank order and rounds to T once. Every CTA takes a
-// ticket once it has read the epoch; the holder of the last one advances the
-// rank's epoch as it exits. A CTA
+// own buffer, sums them in rank order and rounds to T once. One CTA per
+// cluster reads the rank's epoch, hands it to the cluster with its first
+// partial push and takes the cluster's ticket; the holder of the last ticket
+// advances the epoch as it exits. A CTA
 // that waits on a peer's CTAs must not wait behind a wave of its own grid,
 // so this instance launches only when the grid fits in one wave.
 #include <cooperative_groups.h>
@@ -198,7 +199,8 @@ __device__ __forceinline__ void xchg_gather(const FusedArgs& p, bool shrink_on, 
           const unsigned long long w = tagged_word(epoch, v);
 #pragma unroll
           for (int q = 0; q < kMaxPeers; ++q)
-            if (q < xg.tp && q % cs == j && (q != xg.rank || !expand_on)) word_store_sys(xg.recv[q] + at, w);
+            if (q < xg.tp && (q & (cs - 1)) == j && (q != xg.rank || !expand_on))  // cs: a power of two
+              word_store_sys(xg.recv[q] + at, w);
         }
       }
     }
@@ -299,10 +301,9 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? (XCHG ? 4 : 5) : RM == 32
   if (rank == 0 || (sl.n == 0 && p.bs <= kFusedScan)) {
     if (XCHG && p.phase != 1) {
       pdl_trigger();
-      if (tid == 0) {
+      if (j == 0 && tid == 0) {  // the cluster's ticket
         pdl_wait();  // the previous call has finished counting
-        const uint32_t epoch = xchg_epoch(p.xchg);
-        xchg_advance(p.xchg, xchg_ticket(p.xchg, epoch), epoch, gridDim.x * gridDim.y * gridDim.z);
+        xchg_advance(p.xchg, xchg_ticket(p.xchg, xchg_epoch(p.xchg)), gridDim.y * gridDim.z);
       }
     } else {
       pdl_exit_early();
@@ -315,7 +316,8 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? (XCHG ? 4 : 5) : RM == 32
   const bool expand_on = !XCHG || p.phase != 1;
 
   // shared memory: A [R][kp] | B [ob_max][R] | x [TT][kp] | y [TT][ob_max] |
-  //                warp partials [NW][TT][RM] f32 | partials in [cs][TT][RM] f32
+  //                warp partials [NW][TT][RM] f32 | partials in [cs][TT][RM] f32 |
+  //                (XCHG) the epoch, 16 bytes
   const int kp = padded_row(p.ks);
   const int k0 = j * p.ks;                       // multiple of 16
   const int kend = min(p.in_dim, k0 + p.ks);
@@ -369,10 +371,11 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? (XCHG ? 4 : 5) : RM == 32
   cp_async_commit();  // group: this CTA's weights
   pdl_trigger();
   pdl_wait();  // x and y come from earlier kernels
-  const uint32_t epoch = XCHG ? xchg_epoch(p.xchg) : 0u;  // after the wait: the previous call has advanced it
-  const bool counts = XCHG && p.phase != 1 && tid == 0;     // this CTA's ticket in the call's count
-  uint32_t ticket = 0u;
-  bool ticketed = false;
+  // The call's epoch: thread 0 of the cluster's CTA 0 reads it (after the
+  // wait: the previous call has advanced it) and hands it to the cluster in
+  // its first partial push, so the call counts one ticket per cluster.
+  const uint32_t eg = XCHG && j == 0 && tid == 0 ? xchg_epoch(p.xchg) : 0u;
+  uint32_t ticket = 0u;  // the cluster's ticket, taken with the first push
 
   const T* __restrict__ xbase = static_cast<const T*>(p.x);
   T* __restrict__ ybase = static_cast<T*>(m.y);
@@ -473,16 +476,23 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? (XCHG ? 4 : 5) : RM == 32
         }
       }
       __syncthreads();  // warp partials complete
+      const bool epoch_push = XCHG && first;  // the first push carries the epoch
       if (first) cluster_wait_acquire();  // every peer runs and has its barriers initialised
       first = false;
-      if (counts && !ticketed) {  // the epoch load has long returned
-        ticket = xchg_ticket(p.xchg, epoch);
-        ticketed = true;
-      }
+      if (XCHG && epoch_push && j == 0 && tid == 0 && p.phase != 1)
+        ticket = xchg_ticket(p.xchg, eg);  // the epoch load has long returned
       // ---- push this CTA's partial (its warps' partials summed in warp order) into
-      //      slot j of every peer's receive buffer ----
-      if (shrink_on) {  // phase 2 has no shrink
-        if (tid == 0) mbar_arrive_expect_tx(&bar_p, (uint32_t)cs * nt * RM * sizeof(float));
+      //      slot j of every peer's receive buffer (phase 2: zeros, for the epoch) ----
+      {
+        if (tid == 0)
+          mbar_arrive_expect_tx(&bar_p, (uint32_t)cs * nt * RM * sizeof(float) + (epoch_push ? 16u : 0u));
+        if (epoch_push && j == 0 && tid == 0) {  // the epoch, into every CTA's slot after the partials
+          const uint32_t dst = smem_addr(s_recv + (size_t)cs * TT * RM);
+          const uint32_t bar = smem_addr(&bar_p);
+          for (int q = 0; q < cs; ++q)
+            st_async_v4(cluster_map(dst, (uint32_t)q), __uint_as_float(eg), 0.f, 0.f, 0.f,
+                        cluster_map(bar, (uint32_t)q));
+        }
         if (tid < nt * Q4) {
           const int t = tid / Q4, k4 = (tid - t * Q4) * 4;
           float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -503,6 +513,7 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? (XCHG ? 4 : 5) : RM == 32
         p_phase ^= 1u;
       }
       if constexpr (XCHG) {
+        const uint32_t epoch = __float_as_uint(s_recv[(size_t)cs * TT * RM]);
         xchg_gather<T, RM>(p, shrink_on, expand_on, epoch, cs, j, nt, rank, s_recv, s_rows, s_mid, s_xfail);
       } else {
         // ---- gather: mid = sum of the cs partials in CTA order, rounded to T once ----
@@ -629,9 +640,9 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? (XCHG ? 4 : 5) : RM == 32
   if (b_pending) mbar_wait(&bar_w, 0, p.status);
   cp_async_wait<0>();
   if (!ok && tid == 0) mbar_wait(&bar_p, p_phase ^ 1u, p.status);  // ok is only cleared inside a tile
-  if (counts) {
-    if (!ticketed) ticket = xchg_ticket(p.xchg, epoch);  // no tile of this slot in any scan pass
-    xchg_advance(p.xchg, ticket, epoch, gridDim.x * gridDim.y * gridDim.z);
+  if (XCHG && j == 0 && tid == 0 && p.phase != 1) {
+    if (first) ticket = xchg_ticket(p.xchg, xchg_epoch(p.xchg));  // no tile of this slot in any scan pass
+    xchg_advance(p.xchg, ticket, gridDim.y * gridDim.z);
   }
 }
 
@@ -763,7 +774,7 @@ cudaError_t launch_rmx(FusedArgs a, cudaStream_t st, bool pdl) {
       ob_max = m.ob > ob_max ? m.ob : ob_max;
       m.y_tma = (reinterpret_cast<uintptr_t>(m.y) % 16 == 0) && (m.y_stride % 8 == 0) && (m.out_dim % 8 == 0);
     }
-    const size_t smem = fused_smem(c, RM, ks, ob_max, cs);
+    const size_t smem = fused_smem(c, RM, ks, ob_max, cs) + (XCHG ? 16 : 0);  // + the epoch slot
     if (smem > 200 * 1024) continue;
     const int per_sm = l.occupancy(cs, smem);
     if (per_sm <= 0) continue;

@@ -97,11 +97,12 @@ __device__ __forceinline__ uint32_t xchg_ticket(const PeerXchg& x, uint32_t epoc
   if (epoch != 0xFFFFFFFFu) return atomicAdd(&x.ctr[1], 1u);
   return atomicInc(&x.ctr[1], 0xFFFFFFFFu);  // the same increment (the counter never reaches the bound)
 }
-// The holder of the last of `counted` tickets resets the count and advances the epoch.
-__device__ __forceinline__ void xchg_advance(const PeerXchg& x, uint32_t ticket, uint32_t epoch, uint32_t counted) {
+// The holder of the last of `counted` tickets resets the count and advances
+// the epoch (an increment whose result nobody waits for).
+__device__ __forceinline__ void xchg_advance(const PeerXchg& x, uint32_t ticket, uint32_t counted) {
   if (ticket == counted - 1u) {
     x.ctr[1] = 0u;
-    x.ctr[0] = epoch + 1u;
+    atomicAdd(&x.ctr[0], 1u);
   }
 }
 
