@@ -166,6 +166,17 @@ struct FlatWalk {
 // ldmatrix reads conflict-free: an odd number of 16-byte units.
 __host__ __device__ __forceinline__ int padded_row(int k) { return ((k / 8) % 2 == 0) ? k + 8 : k; }
 
+// The exchange's fields, copied from the kernel parameters into the first
+// kXchgSmem bytes of dynamic shared memory when the CTA starts: the gather
+// then reads them without a constant-cache miss on its critical path.
+struct XchgShared {
+  unsigned long long* recv[kMaxPeers];
+  uint32_t* ctr;
+  int tp, rank, rows;
+};
+constexpr int kXchgSmem = 128;
+static_assert(sizeof(XchgShared) <= kXchgSmem, "exchange fields");
+
 // Row-parallel gather of one tile (the XCHG instance): with the shrink on
 // (phases 0 and 1) this rank's partial -- the cluster's cs partials summed in
 // CTA order -- is published to every rank as tagged words, the destinations
@@ -176,13 +187,14 @@ __host__ __device__ __forceinline__ int padded_row(int k) { return ((k / 8) % 2 
 // within the wait limit sets `s_xfail` and the timeout bit; the caller then
 // skips the expand.
 template <typename T, int RM>
-__device__ __forceinline__ void xchg_gather(const FusedArgs& p, bool shrink_on, bool expand_on, uint32_t epoch, int cs,
-                                            int j, int nt, int rank, const float* s_recv, const int* s_rows,
-                                            T (*s_mid)[RM + 8], int& s_xfail) {
+__device__ __forceinline__ void xchg_gather(const XchgShared& xg, int R, uint32_t* status, bool shrink_on,
+                                            bool expand_on, uint32_t epoch, int cs, int j, int nt, int rank,
+                                            const float* s_recv, const int* s_rows, T (*s_mid)[RM + 8],
+                                            int& s_xfail) {
   constexpr int NT = kFusedNT, TT = kFusedTT;
   static_assert(TT * RM <= 2 * NT, "two gather elements per thread");
-  const PeerXchg& xg = p.xchg;
   const int tid = threadIdx.x;
+  const int tp = xg.tp, me = xg.rank, rows = xg.rows;
   float loc[2] = {0.f, 0.f};
   if (shrink_on) {
 #pragma unroll
@@ -194,24 +206,19 @@ __device__ __forceinline__ void xchg_gather(const FusedArgs& p, bool shrink_on, 
         for (int q = 0; q < cs; ++q) v += s_recv[((size_t)q * TT + t) * RM + k];
         loc[i] = v;
         const int row = s_rows[t];
-        if (row < xg.rows) {
-          const int64_t at = xchg_row(xg, epoch, xg.rank, row, p.R) + k;
+        if (row < rows) {
+          const int64_t at = xchg_offset(epoch, tp, rows, me, row, R) + k;
           const unsigned long long w = tagged_word(epoch, v);
-#pragma unroll
-          for (int q = 0; q < kMaxPeers; ++q)
-            if (q < xg.tp && (q & (cs - 1)) == j && (q != xg.rank || !expand_on))  // cs: a power of two
-              word_store_sys(xg.recv[q] + at, w);
+          for (int q = j; q < tp; q += cs)  // this CTA's destinations
+            if (q != me || !expand_on) word_store_sys(xg.recv[q] + at, w);
         }
       }
     }
   }
   if (!expand_on) return;
   const uint32_t tag = epoch + 1u;
-  const unsigned long long* own = xg.recv[0];
-#pragma unroll
-  for (int q = 1; q < kMaxPeers; ++q)
-    if (q == xg.rank) own = xg.recv[q];
-  const int64_t xq = (int64_t)xg.rows * p.R;  // words between two ranks' partial rows
+  const unsigned long long* own = xg.recv[me];
+  const int64_t xq = (int64_t)rows * R;  // words between two ranks' partial rows
   const bool skip = *reinterpret_cast<volatile int*>(&s_xfail) != 0;
   bool good = true;
 #pragma unroll
@@ -220,20 +227,26 @@ __device__ __forceinline__ void xchg_gather(const FusedArgs& p, bool shrink_on, 
     if (e < TT * RM) {
       const int t = e / RM, k = e - t * RM;
       float v = 0.f;
-      if (t < nt && k < rank && !skip && s_rows[t] < xg.rows) {
-        const unsigned long long* base = own + xchg_row(xg, epoch, 0, s_rows[t], p.R) + k;
+      if (t < nt && k < rank && !skip && s_rows[t] < rows) {
+        const unsigned long long* base = own + xchg_offset(epoch, tp, rows, 0, s_rows[t], R) + k;
         unsigned long long wv[kMaxPeers];
 #pragma unroll
         for (int q = 0; q < kMaxPeers; ++q) {  // every load issued before the first poll
           wv[q] = 0ull;
-          if (q < xg.tp && (q != xg.rank || !shrink_on)) wv[q] = word_load(base + q * xq);
+          if (q < tp && (q != me || !shrink_on)) wv[q] = word_load(base + q * xq);
         }
-        uint64_t t0 = 0;
 #pragma unroll
         for (int q = 0; q < kMaxPeers; ++q) {
-          if (q < xg.tp) {
+          if (q < tp) {
             float pq = loc[i];
-            if ((q != xg.rank || !shrink_on) && good) good = poll_word(base + q * xq, wv[q], tag, pq, t0);
+            if (q != me || !shrink_on) {
+              unsigned long long a = wv[q];
+              if ((uint32_t)(a >> 32) != tag && good) {  // not there yet: wait (bounded), out of line
+                a = poll_until(base + q * xq, tag);
+                good = (uint32_t)(a >> 32) == tag;
+              }
+              pq = __uint_as_float((uint32_t)a);
+            }
             v += pq;
           }
         }
@@ -243,7 +256,7 @@ __device__ __forceinline__ void xchg_gather(const FusedArgs& p, bool shrink_on, 
   }
   if (!good) {
     s_xfail = 1;
-    flag_error(p.status, kErrTimeout);
+    flag_error(status, kErrTimeout);
   }
 }
 
@@ -288,6 +301,21 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? (XCHG ? 4 : 5) : RM == 32
       default: s_scale = __ldg(static_cast<const float*>(p.scalings) + slot); break;
     }
   }
+  XchgShared& sx = *reinterpret_cast<XchgShared*>(s_dyn);  // XCHG only
+  if (XCHG && tid >= 64 && tid < 64 + kMaxPeers) {  // warp 2 is idle during the scan
+    const int q = tid - 64;
+    unsigned long long* r = p.xchg.recv[0];
+#pragma unroll
+    for (int i = 1; i < kMaxPeers; ++i)
+      if (q == i) r = p.xchg.recv[i];
+    sx.recv[q] = r;
+  }
+  if (XCHG && tid == 64 + kMaxPeers) {
+    sx.ctr = p.xchg.ctr;
+    sx.tp = p.xchg.tp;
+    sx.rank = p.xchg.rank;
+    sx.rows = p.xchg.rows;
+  }
   fused_scan(sl, slot, 0, p, s_rows);  // also the first tile's token rows
   __syncthreads();
   int rank = s_rank;
@@ -303,7 +331,7 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? (XCHG ? 4 : 5) : RM == 32
       pdl_trigger();
       if (j == 0 && tid == 0) {  // the cluster's ticket
         pdl_wait();  // the previous call has finished counting
-        xchg_advance(p.xchg, xchg_ticket(p.xchg, xchg_epoch(p.xchg)), gridDim.y * gridDim.z);
+        xchg_advance(sx.ctr, xchg_ticket(sx.ctr, load_epoch(sx.ctr)), gridDim.y * gridDim.z);
       }
     } else {
       pdl_exit_early();
@@ -315,7 +343,7 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? (XCHG ? 4 : 5) : RM == 32
   const bool shrink_on = !XCHG || p.phase != 2;
   const bool expand_on = !XCHG || p.phase != 1;
 
-  // shared memory: A [R][kp] | B [ob_max][R] | x [TT][kp] | y [TT][ob_max] |
+  // shared memory: (XCHG) fields [kXchgSmem bytes] | A [R][kp] | B [ob_max][R] | x [TT][kp] | y [TT][ob_max] |
   //                warp partials [NW][TT][RM] f32 | partials in [cs][TT][RM] f32 |
   //                (XCHG) the epoch, 16 bytes
   const int kp = padded_row(p.ks);
@@ -326,7 +354,7 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? (XCHG ? 4 : 5) : RM == 32
   const int o_lo = min(m.out_dim, j * m.ob);
   const int o_hi = min(m.out_dim, o_lo + m.ob);
   const int olen = o_hi - o_lo;
-  T* s_a = reinterpret_cast<T*>(s_dyn);
+  T* s_a = reinterpret_cast<T*>(s_dyn + (XCHG ? kXchgSmem : 0));
   T* s_b = s_a + (size_t)R * kp;
   T* s_x = s_b + (size_t)p.ob_max * R;
   T* s_y = s_x + (size_t)TT * kp;
@@ -374,7 +402,7 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? (XCHG ? 4 : 5) : RM == 32
   // The call's epoch: thread 0 of the cluster's CTA 0 reads it (after the
   // wait: the previous call has advanced it) and hands it to the cluster in
   // its first partial push, so the call counts one ticket per cluster.
-  const uint32_t eg = XCHG && j == 0 && tid == 0 ? xchg_epoch(p.xchg) : 0u;
+  const uint32_t eg = XCHG && j == 0 && tid == 0 ? load_epoch(sx.ctr) : 0u;
   uint32_t ticket = 0u;  // the cluster's ticket, taken with the first push
 
   const T* __restrict__ xbase = static_cast<const T*>(p.x);
@@ -480,7 +508,7 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? (XCHG ? 4 : 5) : RM == 32
       if (first) cluster_wait_acquire();  // every peer runs and has its barriers initialised
       first = false;
       if (XCHG && epoch_push && j == 0 && tid == 0 && p.phase != 1)
-        ticket = xchg_ticket(p.xchg, eg);  // the epoch load has long returned
+        ticket = xchg_ticket(sx.ctr, eg);  // the epoch load has long returned
       // ---- push this CTA's partial (its warps' partials summed in warp order) into
       //      slot j of every peer's receive buffer (phase 2: zeros, for the epoch) ----
       {
@@ -514,7 +542,8 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? (XCHG ? 4 : 5) : RM == 32
       }
       if constexpr (XCHG) {
         const uint32_t epoch = __float_as_uint(s_recv[(size_t)cs * TT * RM]);
-        xchg_gather<T, RM>(p, shrink_on, expand_on, epoch, cs, j, nt, rank, s_recv, s_rows, s_mid, s_xfail);
+        xchg_gather<T, RM>(sx, R, p.status, shrink_on, expand_on, epoch, cs, j, nt, rank, s_recv, s_rows, s_mid,
+                           s_xfail);
       } else {
         // ---- gather: mid = sum of the cs partials in CTA order, rounded to T once ----
         for (int e = tid; e < TT * RM; e += NT) {
@@ -641,8 +670,8 @@ __global__ void __launch_bounds__(kFusedNT, RM == 16 ? (XCHG ? 4 : 5) : RM == 32
   cp_async_wait<0>();
   if (!ok && tid == 0) mbar_wait(&bar_p, p_phase ^ 1u, p.status);  // ok is only cleared inside a tile
   if (XCHG && j == 0 && tid == 0 && p.phase != 1) {
-    if (first) ticket = xchg_ticket(p.xchg, xchg_epoch(p.xchg));  // no tile of this slot in any scan pass
-    xchg_advance(p.xchg, ticket, gridDim.y * gridDim.z);
+    if (first) ticket = xchg_ticket(sx.ctr, load_epoch(sx.ctr));  // no tile of this slot in any scan pass
+    xchg_advance(sx.ctr, ticket, gridDim.y * gridDim.z);
   }
 }
 
@@ -774,7 +803,7 @@ cudaError_t launch_rmx(FusedArgs a, cudaStream_t st, bool pdl) {
       ob_max = m.ob > ob_max ? m.ob : ob_max;
       m.y_tma = (reinterpret_cast<uintptr_t>(m.y) % 16 == 0) && (m.y_stride % 8 == 0) && (m.out_dim % 8 == 0);
     }
-    const size_t smem = fused_smem(c, RM, ks, ob_max, cs) + (XCHG ? 16 : 0);  // + the epoch slot
+    const size_t smem = fused_smem(c, RM, ks, ob_max, cs) + (XCHG ? kXchgSmem + 16 : 0);  // + fields, epoch slot
     if (smem > 200 * 1024) continue;
     const int per_sm = l.occupancy(cs, smem);
     if (per_sm <= 0) continue;

@@ -39,9 +39,13 @@ __device__ __forceinline__ unsigned long long tagged_word(uint32_t epoch, float 
 __device__ __forceinline__ uint32_t xchg_epoch(const PeerXchg& x) {
   return *reinterpret_cast<volatile const uint32_t*>(x.ctr);
 }
-// Offset (words) of partial row `row` from rank `from` in a receive buffer.
+// Offset (words) of partial row `row` from rank `from` in a receive buffer
+// of `tp` ranks x `rows` rows x R words per half.
+__device__ __forceinline__ int64_t xchg_offset(uint32_t epoch, int tp, int rows, int from, int row, int R) {
+  return ((int64_t)(epoch & 1u) * tp * rows + (int64_t)from * rows + row) * R;
+}
 __device__ __forceinline__ int64_t xchg_row(const PeerXchg& x, uint32_t epoch, int from, int row, int R) {
-  return ((int64_t)(epoch & 1u) * x.tp * x.rows + (int64_t)from * x.rows + row) * R;
+  return xchg_offset(epoch, x.tp, x.rows, from, row, R);
 }
 // Polls the word at `w` (already loaded once into `a`) until it carries
 // `tag`; bounded by kWaitLimitNs from `t0` (0: not started). Returns false
@@ -55,6 +59,16 @@ __device__ __forceinline__ bool poll_word(const unsigned long long* w, unsigned 
   }
   v = __uint_as_float((uint32_t)a);
   return true;
+}
+// Slow path of a poll, kept out of line (the common case, a word that has
+// already arrived, costs a tag compare in the caller): reloads the word at
+// `w` until it carries `tag` or kWaitLimitNs have passed; returns the last
+// word read (the caller checks its tag).
+static __device__ __noinline__ unsigned long long poll_until(const unsigned long long* w, uint32_t tag) {
+  const uint64_t t0 = global_timer_ns();
+  unsigned long long a = word_load(w);
+  while ((uint32_t)(a >> 32) != tag && global_timer_ns() - t0 <= kWaitLimitNs) a = word_load(w);
+  return a;
 }
 // Two adjacent words (columns c, c + 1 of one rank's row), polled until both
 // carry `tag` (each column only if it is below `live`); bounded by
@@ -93,17 +107,19 @@ __device__ __forceinline__ void xchg_cta_done(const PeerXchg& x, uint32_t counte
 // atomic's round trip hides behind the CTA's work. Nothing needs a fence: the
 // next call reads the counters after griddepcontrol.wait, which makes this
 // grid's stores visible.
-__device__ __forceinline__ uint32_t xchg_ticket(const PeerXchg& x, uint32_t epoch) {
-  if (epoch != 0xFFFFFFFFu) return atomicAdd(&x.ctr[1], 1u);
-  return atomicInc(&x.ctr[1], 0xFFFFFFFFu);  // the same increment (the counter never reaches the bound)
+// (`ctr`: the rank's counters, PeerXchg::ctr.)
+__device__ __forceinline__ uint32_t xchg_ticket(uint32_t* ctr, uint32_t epoch) {
+  if (epoch != 0xFFFFFFFFu) return atomicAdd(&ctr[1], 1u);
+  return atomicInc(&ctr[1], 0xFFFFFFFFu);  // the same increment (the counter never reaches the bound)
 }
 // The holder of the last of `counted` tickets resets the count and advances
 // the epoch (an increment whose result nobody waits for).
-__device__ __forceinline__ void xchg_advance(const PeerXchg& x, uint32_t ticket, uint32_t counted) {
+__device__ __forceinline__ void xchg_advance(uint32_t* ctr, uint32_t ticket, uint32_t counted) {
   if (ticket == counted - 1u) {
-    x.ctr[1] = 0u;
-    atomicAdd(&x.ctr[0], 1u);
+    ctr[1] = 0u;
+    atomicAdd(&ctr[0], 1u);
   }
 }
+__device__ __forceinline__ uint32_t load_epoch(const uint32_t* ctr) { return *reinterpret_cast<volatile const uint32_t*>(ctr); }
 
 }  // namespace mlora
