@@ -570,14 +570,22 @@ __global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(cons
   const int g = lane >> 2, cq = lane & 3;
   const int brow = lane & 7, bhalf = (lane >> 3) & 1;
   bool ok = true;
-  uint32_t epoch = 0;
-  if (xchg) {
+  // exchange: thread 0 reads the call's epoch (after the wait: the previous
+  // call has advanced it), takes this CTA's ticket in the call's count right
+  // away (the atomic waits for the load; its result is used only at exit) and
+  // hands the epoch to the consumers
+  __shared__ uint32_t s_epoch;
+  uint32_t ticket = 0u;
+  if (xchg && tid == 0) {
     pdl_wait();
-    epoch = xchg_epoch(p.xchg);
+    s_epoch = load_epoch(p.xchg.ctr);
+    ticket = xchg_ticket(p.xchg.ctr, s_epoch);
   }
   __shared__ int s_xfail;  // exchange: a lane's poll ran out (the item is skipped, stages still drained)
   if (tid == 0) s_xfail = 0;
   named_barrier(1, NC * 32);
+  if (xchg) pdl_wait();  // (thread 0 waited already) mid and y come from earlier kernels
+  const uint32_t epoch = xchg ? s_epoch : 0u;
   bool xgood = true;
   for (int j = 0; j < my_items; ++j) {
     const int s = j % NS;
@@ -754,7 +762,7 @@ __global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(cons
   }
   if (tid == 0) {
     bulk_wait_all();
-    if (xchg) xchg_cta_done(p.xchg, (uint32_t)min(G, n_items));
+    if (xchg) xchg_advance(p.xchg.ctr, ticket, (uint32_t)min(G, n_items));
   }
 }
 

@@ -87,19 +87,6 @@ __device__ __forceinline__ bool poll_pair(const unsigned long long* w, uint32_t 
   v1 = need1 ? __uint_as_float((uint32_t)b) : 0.f;
   return true;
 }
-// Counts the CTAs of the call's last kernel (`counted` of them take part);
-// the last one advances the epoch. Every counted CTA read the epoch after its
-// griddepcontrol.wait (or never reads it), and that wait already implies the
-// previous call's last kernel completed, so two calls never count at once.
-__device__ __forceinline__ void xchg_cta_done(const PeerXchg& x, uint32_t counted) {
-  __threadfence();
-  if (atomicAdd(&x.ctr[1], 1u) == counted - 1u) {
-    x.ctr[1] = 0u;
-    x.ctr[0] = x.ctr[0] + 1u;
-    __threadfence();
-  }
-}
-
 // A CTA's ticket in the count of the call's last kernel, taken once the CTA
 // has read the epoch: both branches depend on the loaded value, so the atomic
 // cannot overtake the load (the epoch this CTA uses is the one before any
