@@ -275,6 +275,10 @@ int mlora_peer_buffer_destroy(void* buffer);
  * 2 = wait and expand only. Phases 1 and 2 let one process drive several
  * ranks' exchanges on ONE GPU (every rank's phase 1 before any rank's phase 2),
  * so that no kernel ever waits for a kernel queued after it.
+ * Kernels: decode batches (rows < 256, meta->max_len <= 16) run one fused
+ * launch (shrink, exchange, expand) when its grid fits in one wave, other
+ * shapes the streaming shrink/expand pair; mlora_last_apply_path() returns 1
+ * or 3 accordingly and mlora_set_apply_path() can force either.
  * Shape range: bf16/f16, in_shard % 16 == 0, max_rank % 8 == 0 and <= 64,
  * out_cols % 8 == 0, 16-byte aligned operands; otherwise
  * MLORA_ERR_INVALID_ARGUMENT (use the NCCL path).
