@@ -6,7 +6,7 @@
 * two or more GPUs: one process per GPU over NCCL through
   ``row_parallel_apply`` (skipped when the box has one GPU), with the
   partials summed by an NCCL all-reduce and by the peer-memory exchange;
-* the peer-memory exchange with 2 and 4 ranks emulated on one GPU (every
+* the peer-memory exchange with 2, 4 and 8 ranks emulated on one GPU (every
   rank's shrink-and-publish phase, then every rank's wait-and-expand phase, so
   no kernel waits for one queued after it), repeated calls, inside a CUDA
   graph, one rank's single-launch call between the others' two phases, and
@@ -156,7 +156,7 @@ def _p2p_call(bes, ranks, xs, y_parts, path=None):
 
 
 @pytest.mark.parametrize("path", sorted(PATHS))
-@pytest.mark.parametrize("tp", [2, 4])
+@pytest.mark.parametrize("tp", [2, 4, 8])
 def test_p2p_exchange_emulated_one_gpu(cuda_dev, tp, path):
     """Sum over ranks of the pre-all-reduce outputs = the unsharded delta; three
     calls in a row (epochs 1..3, both halves of the double-buffered partials)."""
@@ -213,7 +213,7 @@ def test_p2p_exchange_in_cuda_graph(cuda_dev, path):
 
 
 @pytest.mark.parametrize("path", sorted(PATHS))
-@pytest.mark.parametrize("tp", [2, 4])
+@pytest.mark.parametrize("tp", [2, 4, 8])
 def test_p2p_single_launch_between_phases(cuda_dev, tp, path):
     """Rank 0 runs the whole call in one go (phase 0: publish, wait, expand)
     after every other rank published and before they expand, so its waits
