@@ -482,6 +482,7 @@ int mlora_rmsnorm_fwd(const void* x, int64_t rows, int64_t hidden, int64_t strid
   const int V = 16 / es;
   a.vec_ok = (hidden % V == 0) && (stride_outer % V == 0) && (stride_inner % V == 0) && (y_row_stride % V == 0) &&
              aligned(x, 16) && aligned(y, 16);
+  a.w_vec = aligned(w, 16);
   return cuda_status(mlora::launch_rmsnorm(a, dtype, (cudaStream_t)stream, pdl_on()), "rmsnorm launch");
 }
 
@@ -518,6 +519,7 @@ int mlora_fused_add_rmsnorm_fwd(const void* x, int64_t x_row_stride, void* resid
   const int V = 16 / es;
   a.vec_ok = (hidden % V == 0) && (x_row_stride % V == 0) && (residual_row_stride % V == 0) &&
              (y_row_stride % V == 0) && aligned(x, 16) && aligned(residual, 16) && aligned(y, 16);
+  a.w_vec = aligned(w, 16);
   return cuda_status(mlora::launch_rmsnorm(a, dtype, (cudaStream_t)stream, pdl_on()), "fused add + rmsnorm launch");
 }
 

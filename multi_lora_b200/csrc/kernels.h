@@ -59,6 +59,7 @@ struct RmsNormArgs {
   int hidden;
   float eps;
   int vec_ok;
+  int w_vec;              // w 16-byte aligned: its chunks load as vectors
   // fused add (optional): row r of x is first replaced by T(x[r] + add[r]),
   // written to res + r * res_stride, and that rounded sum is normalised
   const void* add;        // nullptr: plain RMSNorm

@@ -241,6 +241,31 @@ def test_p2p_single_launch_between_phases(cuda_dev, tp, path):
         xs[0].close()
 
 
+def test_p2p_fused_declines_grids_over_one_wave(cuda_dev):
+    """The fused exchange kernel's CTAs wait on other ranks' CTAs, so it runs
+    only when its whole grid is resident at once. With 512 slots (at least
+    1024 CTAs, while the exchange instance's register cap leaves at most 4
+    CTAs on each of 148 SMs) it declines and the streaming pair runs the
+    call, even when the fused path is forced."""
+    dev = cuda_dev
+    c = _case(seed=9, K=512)
+    tp = 2
+    bes, ranks = _p2p_setup(dev, tp, c)
+    xs = PeerExchange.local_group(tp, device=dev, max_rows=64, max_rank=16)
+    ref = torch.from_numpy(_ref_delta(c))
+    try:
+        y_parts = [torch.zeros(c["y"].shape, dtype=torch.bfloat16, device=dev) for _ in range(tp)]
+        with forced_path("fused"):
+            _p2p_call(bes, ranks, xs, y_parts, "stream")
+        torch.cuda.synchronize()
+        delta = torch.stack([y.float() for y in y_parts]).sum(0).cpu()
+        torch.testing.assert_close(delta, ref, **TOL)
+        for be in bes:
+            be.check_routing()
+    finally:
+        xs[0].close()
+
+
 @pytest.mark.parametrize("path", sorted(PATHS))
 def test_p2p_exchange_wait_times_out_and_reports(cuda_dev, path):
     """A rank whose peer never publishes: its bounded polls run out (about 2 s),
