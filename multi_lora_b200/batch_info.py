@@ -56,15 +56,20 @@ def segment_lens(bs: int, seq_lens: List[int]) -> Tuple[List[int], List[int]]:
 
     ``seq_lens == []`` means decode: every segment is one token.
     """
-    if seq_lens:
+    lens, indptr = _segment_arrays(bs, seq_lens)
+    return lens.tolist(), indptr.tolist()
+
+
+def _segment_arrays(bs: int, seq_lens: List[int]) -> Tuple[np.ndarray, np.ndarray]:
+    """``segment_lens`` as int64 arrays (the per-step write path)."""
+    if len(seq_lens):
         if len(seq_lens) != bs:
             raise AssertionError(f"seq_lens needs one entry per segment: {len(seq_lens)} vs {bs}")
-        lens = [int(n) for n in seq_lens]
+        lens = np.asarray(seq_lens, dtype=np.int64)
     else:
-        lens = [1] * bs
-    indptr = [0] * (len(lens) + 1)
-    for i, n in enumerate(lens):
-        indptr[i + 1] = indptr[i] + n
+        lens = np.ones(bs, dtype=np.int64)
+    indptr = np.zeros(bs + 1, dtype=np.int64)
+    np.cumsum(lens, out=indptr[1:])
     return lens, indptr
 
 
@@ -135,6 +140,8 @@ class _PackedColumns:
         pin = self.device.type == "cuda"
         self.host = torch.zeros(self.words, dtype=torch.int32, pin_memory=pin)
         self.copy_done: Optional[torch.cuda.Event] = None
+        self._scal_src: Optional[list] = None  # scalings last converted, and their words
+        self._scal_words: Optional[np.ndarray] = None
 
     def views(self):
         d = self.dev
@@ -157,11 +164,14 @@ class _PackedColumns:
         h[self.o_widx: self.o_widx + len(widx)] = widx
         h[self.o_ranks: self.o_ranks + k] = 0
         h[self.o_ranks: self.o_ranks + len(ranks)] = ranks
-        es = torch.empty(0, dtype=self.dtype).element_size()
-        scal = torch.zeros(self.scal_words * 4 // es, dtype=self.dtype)
-        if scalings:
-            scal[: len(scalings)] = torch.tensor(scalings, dtype=torch.float64).to(self.dtype)
-        h[self.o_scal: self.o_scal + self.scal_words] = scal.view(torch.int32).numpy()
+        scalings = list(scalings)
+        if scalings != self._scal_src:  # converted again only when they change
+            es = torch.empty(0, dtype=self.dtype).element_size()
+            scal = torch.zeros(self.scal_words * 4 // es, dtype=self.dtype)
+            if scalings:
+                scal[: len(scalings)] = torch.tensor(scalings, dtype=torch.float64).to(self.dtype)
+            self._scal_src, self._scal_words = scalings, scal.view(torch.int32).numpy().copy()
+        h[self.o_scal: self.o_scal + self.scal_words] = self._scal_words
         if self.device.type == "cuda":
             self.dev.copy_(self.host, non_blocking=True)
             if self.copy_done is None:
@@ -171,20 +181,24 @@ class _PackedColumns:
             self.dev.copy_(self.host)
 
 
-def _validate(pool_batch: BatchLoRAInfo, lens: List[int]) -> None:
-    """Host-side routing checks, done before the lists leave the host."""
+def _validate(pool_batch: BatchLoRAInfo, lens: np.ndarray) -> Tuple[np.ndarray, np.ndarray]:
+    """Host-side routing checks, done before the lists leave the host; returns
+    weight_indices and lora_ranks as int64 arrays."""
     k = len(pool_batch.lora_ranks)
     if len(pool_batch.scalings) != k:
         raise ValueError(f"scalings has {len(pool_batch.scalings)} entries, lora_ranks {k}")
-    for i, s in enumerate(pool_batch.weight_indices):
-        if not 0 <= int(s) < k:
-            raise ValueError(f"weight_indices[{i}] = {s} outside [0, {k})")
-    for s, r in enumerate(pool_batch.lora_ranks):
-        if int(r) < 0:
-            raise ValueError(f"lora_ranks[{s}] = {r} is negative")
-    for i, n in enumerate(lens):
-        if n < 0:
-            raise ValueError(f"segment {i} has negative length {n}")
+    widx = np.asarray(pool_batch.weight_indices, dtype=np.int64).reshape(-1)
+    if widx.size and (widx.min() < 0 or widx.max() >= k):  # the first offender is named
+        i = int(np.flatnonzero((widx < 0) | (widx >= k))[0])
+        raise ValueError(f"weight_indices[{i}] = {pool_batch.weight_indices[i]} outside [0, {k})")
+    ranks = np.asarray(pool_batch.lora_ranks, dtype=np.int64).reshape(-1)
+    if ranks.size and ranks.min() < 0:
+        s = int(np.flatnonzero(ranks < 0)[0])
+        raise ValueError(f"lora_ranks[{s}] = {pool_batch.lora_ranks[s]} is negative")
+    if lens.size and lens.min() < 0:
+        i = int(np.flatnonzero(lens < 0)[0])
+        raise ValueError(f"segment {i} has negative length {int(lens[i])}")
+    return widx, ranks
 
 
 def write_kernel_input_metadata(
@@ -202,9 +216,9 @@ def write_kernel_input_metadata(
     scalings always have one entry per pool slot.
     """
     rows = len(pool_batch.weight_indices)
-    lens, indptr = segment_lens(rows, seq_lens)
-    _validate(pool_batch, lens)
-    max_len = max(lens) if lens else 0
+    lens, indptr = _segment_arrays(rows, seq_lens)
+    widx, ranks = _validate(pool_batch, lens)
+    max_len = int(lens.max()) if rows else 0
     if rows > meta.weight_indices.shape[0]:
         # does not fit: new tables sized for this batch
         packed = _PackedColumns(rows, len(pool_batch.lora_ranks), device, dtype)
@@ -213,17 +227,17 @@ def write_kernel_input_metadata(
                                    lora_ranks=cols[3], scalings=cols[4], max_len=max_len, _packed=packed)
     elif meta._packed is None:
         # user-built metadata with room: column-by-column refresh, as the reference does
-        fill_column(meta.weight_indices, pool_batch.weight_indices, 0)
-        fill_column(meta.lora_ranks, pool_batch.lora_ranks, 0)
-        fill_column(meta.seg_lens, lens, 0)
-        fill_column(meta.seg_indptr, indptr, indptr[-1])
+        fill_column(meta.weight_indices, widx.tolist(), 0)
+        fill_column(meta.lora_ranks, ranks.tolist(), 0)
+        fill_column(meta.seg_lens, lens.tolist(), 0)
+        fill_column(meta.seg_indptr, indptr.tolist(), int(indptr[-1]))
         fill_column(meta.scalings, pool_batch.scalings, 0.0)
         meta.bs, meta.max_len = rows, max_len
         return meta
     packed = meta._packed
     if len(pool_batch.lora_ranks) > packed.k:
         raise AssertionError(f"{len(pool_batch.lora_ranks)} slots do not fit {packed.k} entries")
-    packed.write(lens, indptr, pool_batch.weight_indices, pool_batch.lora_ranks, pool_batch.scalings)
+    packed.write(lens, indptr, widx, ranks, pool_batch.scalings)
     meta.bs = rows
     meta.max_len = max_len
     return meta
