@@ -19,7 +19,7 @@
 //     the rounded mid rows go to the caller's mid buffer (columns < rank).
 //   expand kernel: item = (tile, projection, OC-row block of B); it streams
 //     B[slot, block, :], the tile's y rows (block columns) and mid rows, and
-//     writes the updated y rows back with one bulk store per row.
+//     writes the updated y values straight from registers to the caller's rows.
 // One producer warp fills a kStreamStages-deep shared-memory ring with 1-D
 // TMA bulk copies (lane 0 arms the stage's full mbarrier with the byte count,
 // the lanes issue one row copy each: a single issuing thread was measured at
@@ -686,12 +686,17 @@ __global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(cons
           }
         }
       };
+      // y = T(T(scale * acc) + y): read from the staged tile, written straight
+      // to the caller's row (token g of the tile), so the stage is free as soon
+      // as this warp has computed
+      T* const yg = static_cast<T*>(it.m.y) + (int64_t)rt.tok[it.t.start + (g < nt ? g : 0)] * it.m.y_stride + it.o0;
       auto tile_store = [&](int nb, const float (&acc)[4]) {
-        if (g < nt) {  // y = T(T(scale * acc) + y), in place in the staged tile
-          uint32_t* yp = reinterpret_cast<uint32_t*>(ys + g * OCP + nb * 8 + 2 * cq);
-          const uint32_t u = *yp;
+        if (g < nt) {
+          const int o = nb * 8 + 2 * cq;
+          const uint32_t u = *reinterpret_cast<const uint32_t*>(ys + g * OCP + o);
           const uint32_t d = pack_round2<T>(acc[0] * scale, acc[1] * scale);  // T(scaling * delta)
-          *yp = pack_round2<T>(Pack2<T>::lo(d) + Pack2<T>::lo(u), Pack2<T>::hi(d) + Pack2<T>::hi(u));
+          *reinterpret_cast<uint32_t*>(yg + o) =
+              pack_round2<T>(Pack2<T>::lo(d) + Pack2<T>::lo(u), Pack2<T>::hi(d) + Pack2<T>::hi(u));
         }
       };
       const int ntl = compute ? it.ocl / 8 : 0;  // nothing written for a skipped item
@@ -702,7 +707,8 @@ __global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(cons
         // tensor-core chains overlap their latencies.
         const uint32_t tile_bytes = 8u * (uint32_t)p.R * sizeof(T);
         uint32_t bad = ba + (uint32_t)((warp * 8 + brow) * p.R + bhalf * 8) * 2u;
-        T* yl = ys + g * OCP + warp * 8 + 2 * cq;
+        const T* yl = ys + g * OCP + warp * 8 + 2 * cq;
+        T* yo = yg + warp * 8 + 2 * cq;
         const bool lane_out = g < nt;
         auto mma_at = [&](uint32_t baddr, float (&acc)[4]) {
           acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
@@ -715,11 +721,11 @@ __global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(cons
             }
           }
         };
-        auto store_at = [&](T* y, const float (&acc)[4]) {  // y = T(T(scale * acc) + y), in place
-          uint32_t* yp = reinterpret_cast<uint32_t*>(y);
-          const uint32_t u = *yp;
+        auto store_at = [&](T* y, const T* sy, const float (&acc)[4]) {  // y = T(T(scale * acc) + y)
+          const uint32_t u = *reinterpret_cast<const uint32_t*>(sy);
           const uint32_t d = pack_round2<T>(acc[0] * scale, acc[1] * scale);
-          *yp = pack_round2<T>(Pack2<T>::lo(d) + Pack2<T>::lo(u), Pack2<T>::hi(d) + Pack2<T>::hi(u));
+          *reinterpret_cast<uint32_t*>(y) =
+              pack_round2<T>(Pack2<T>::lo(d) + Pack2<T>::lo(u), Pack2<T>::hi(d) + Pack2<T>::hi(u));
         };
         for (int nb = warp; nb < ntl; nb += 2 * NC) {
           float acc0[4], acc1[4];
@@ -727,11 +733,12 @@ __global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(cons
           mma_at(bad, acc0);
           if (two) mma_at(bad + NC * tile_bytes, acc1);
           if (lane_out) {
-            store_at(yl, acc0);
-            if (two) store_at(yl + 8 * NC, acc1);
+            store_at(yo, yl, acc0);
+            if (two) store_at(yo + 8 * NC, yl + 8 * NC, acc1);
           }
           bad += 2 * NC * tile_bytes;
           yl += 16 * NC;
+          yo += 16 * NC;
         }
       } else {
         // two output tiles per iteration: independent tensor-core chains overlap their latencies
@@ -745,23 +752,9 @@ __global__ void __launch_bounds__(kStreamThreads) lora_expand_stream_kernel(cons
         }
       }
     }
-    fence_proxy_async_smem();  // the y tile written above is read next by the bulk stores
-    named_barrier(1, NC * 32);
-    // Warp 0 writes the tile back, lane r the row of token r (one bulk store
-    // each, issued side by side: one thread issuing them all serialised ~80 ns
-    // per row in front of the stage's release); each lane waits until its own
-    // store has read the stage, which may then be refilled.
-    if (warp == 0 && ok && xgood && lane < nt) {
-      T* y = static_cast<T*>(it.m.y) + it.o0;
-      bulk_copy_s2g(y + (int64_t)rt.tok[it.t.start + lane] * it.m.y_stride, stage_y(s) + lane * OCP,
-                    it.ocl * sizeof(T));
-      bulk_commit();
-      bulk_wait_read_all();
-    }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
+    if (lane == 0) mbar_arrive(&empty[s]);  // this warp has read the stage
   }
-  if (warp == 0) bulk_wait_all();  // every lane's stores complete before the CTA leaves
   if (xchg && tid == 0) xchg_advance(p.xchg.ctr, ticket, (uint32_t)min(G, n_items));
 }
 
