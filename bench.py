@@ -796,7 +796,10 @@ def main() -> None:
                   + ("exchanged over peer memory (row)" if exchange is not None else "NCCL-all-reduced (row)"))
     else:
         kernel = APPLY_KERNELS.get(path, "unknown")
-    traffic = read_traffic().get(kernel) if wl.name == "cfg2" and tp == 1 else None
+    # ncu DRAM bytes per launch of this workload's kernel(s), one GPU only
+    tr = read_traffic()
+    traffic = (tr.get(f"{wl.name}:{kernel}", tr.get(kernel) if wl.name == "cfg2" else None)
+               if tp == 1 else None)
     step_bytes = ab["lora"] + ab["rmsnorm"]
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                 "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": traffic, "kernel": kernel,
