@@ -10,7 +10,8 @@
 // rows past the segment are computed but never stored).
 //   lora_shrink_tc_kernel: one CTA per (tile, K split). TMA streams 64-column blocks of x
 //     (128 x 64) and of every projection's A[slot] (R x 64) through a
-//     3-4 stage ring in the 128-byte-swizzled K-major layout; one thread issues
+//     2-stage ring in the 128-byte-swizzled K-major layout (two CTAs per SM);
+//     one thread issues
 //     tcgen05.mma (M = 128, N = n_proj * 64, K = 16) into a TMEM accumulator;
 //     every stage is released by tcgen05.commit. The epilogue reads TMEM row
 //     by row (thread = token), rounds to T once and writes mid columns < rank.
@@ -487,12 +488,19 @@ bool ensure_smem_tc(K kern, int bytes) {
 template <typename T, int RT>
 cudaError_t launch_prefill_t(PrefillArgs& a, cudaStream_t st, bool pdl) {
   const int nm = a.n_mod;
-  a.tc_stages = nm * RT <= 128 ? 4 : 3;
-  const int shrink_smem = a.tc_stages * (kTcTileM * kTcBK * 2 + nm * RT * kTcBK * 2) + 1024;
+  // Shrink: two-stage rings, sized so that two CTAs share an SM (with more K
+  // splits, below) -- more bytes in flight per SM than one CTA with a deeper
+  // ring. The ring's shared memory also holds the fp32 partial tile of the
+  // K-split reduction, so it is at least that large.
+  a.tc_stages = 2;
+  const int ring = a.tc_stages * (kTcTileM * kTcBK * 2 + nm * RT * kTcBK * 2);
+  const int part = kTcTileM * (nm * RT + 4) * 4;
+  const int shrink_smem = (ring > part ? ring : part) + 1024;
   const int expand_smem = (kTcTileM * RT * 2) + (kTcBN * RT * 2) + 2 * (kTcTileM * kTcBK * 2) + 1024;
   auto ks = lora_shrink_tc_kernel<T, RT>;
   auto ke = lora_expand_tc_kernel<T, RT>;
-  // the largest shrink configuration of this RT (3 or 4 stages of x + four projections' A blocks)
+  // at least the largest shrink launched at this RT (four projections: the larger of
+  // the 2-stage ring and the K-split partial tile)
   static const bool smem_ok =
       ensure_smem_tc(ks, (4 * RT <= 128 ? 4 : 3) * (kTcTileM * kTcBK * 2 + 4 * RT * kTcBK * 2) + 1024) &&
       ensure_smem_tc(ke, expand_smem);
@@ -501,8 +509,8 @@ cudaError_t launch_prefill_t(PrefillArgs& a, cudaStream_t st, bool pdl) {
   if (tiles > 65535) return cudaErrorNotSupported;
   int blocks = 0;
   for (int m = 0; m < nm; ++m) blocks += (a.mod[m].out_dim + kTcBN - 1) / kTcBN;
-  // K splits: enough shrink CTAs for one per SM, at least 4 K blocks each, a cluster of <= 8
-  int splits = (int)(tc_sm_count() / tiles);
+  // K splits: enough shrink CTAs for two per SM, at least 4 K blocks each, a cluster of <= 8
+  int splits = (int)(2 * tc_sm_count() / tiles);
   splits = splits < 1 ? 1 : splits > 8 ? 8 : splits;
   while (splits > 1 && a.in_dim / kTcBK < 4 * splits) --splits;
   cudaLaunchConfig_t cfg = {};
