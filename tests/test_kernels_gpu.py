@@ -314,6 +314,14 @@ def test_tc_apply_matches_oracle(cuda_dev, dtype, shape):
     _check_apply(c, cuda_dev, dtype, expect_path=4)
 
 
+@pytest.mark.parametrize("lens", [[128, 100] * 80, [200, 64] * 30], ids=["160_tiles_1_split", "90_tiles_2_splits"])
+def test_tc_apply_many_tiles(cuda_dev, lens):
+    """Many prefill tiles: the shrink's K split falls to 1 (a grid of more than one wave of
+    two-per-SM CTAs) or 2, where the small cases above run 3-8 way splits."""
+    c = _case(31, torch.bfloat16, 512, 384, 64, [64, 40, 16], lens, cuda_dev)
+    _check_apply(c, cuda_dev, torch.bfloat16, expect_path=4)
+
+
 @pytest.mark.parametrize("R, ranks", [(64, [64, 8, 33]), (16, [16, 8, 13]), (32, [32, 32, 24])])
 def test_tc_group_matches_separate_projections(cuda_dev, R, ranks):
     """q/k/v-like group on the tensor-core pair: mid [S, 3R] holds one column block per projection."""
